@@ -1,0 +1,161 @@
+/*
+ * fastmka_b200.h — C ABI of the B200 (sm_100a) FastMKA attention forward.
+ *
+ * Every entry point takes device pointers, sizes and element strides, an
+ * explicit cudaStream_t, and returns an int status (FMKA_OK == 0). On failure
+ * fmka_get_last_error() returns the message of the calling thread's last error.
+ * The caller owns every buffer; scratch memory ("workspace") is passed in by the
+ * caller with its size, and each *_workspace_size() function reports how much a
+ * call needs. No entry point allocates device memory; kernels report bounded-
+ * wait timeouts through a status word that lives in the library's own device
+ * data. Calls on distinct streams with distinct buffers may run concurrently.
+ *
+ * bf16 tensors are passed as `void*` holding __nv_bfloat16 values. Layout names:
+ *   [B, T, D]        token rows, element strides (sb, st), channels contiguous
+ *   [B, H, T, 128]   head-split K/V/Q, element strides (sb, sh, st), dims contiguous
+ *
+ * The entry points replace these reference interfaces (FastLM/MKA):
+ *   fmka_qr_proj            q = wq(x) and the router's first layer
+ *                           (mka/layers/fastmka.py:79,91; mka/hf/attention.py:95,104)
+ *   fmka_route_ema_blend    causal_prefix_ema, repeat_retrieval_to_length, the gate
+ *                           softmax and the route blend
+ *                           (mka/layers/session_memory.py:6-39;
+ *                            mka/layers/fastmka.py:82-96; mka/hf/attention.py:97-107)
+ *   fmka_kv_proj            k/v projection of the fused memory (+ RoPE on k)
+ *                           (mka/layers/fastmka.py:98-99; mka/hf/attention.py:110-119)
+ *   fmka_attn_fwd_prefill   causal attention: fastmka_attn (mka/cuda/ops.py:73,
+ *                           mka/cuda/fastmka_attn.cpp:11-17, fastmka_attn.cu:133-172)
+ *                           and the SDPA calls at fastmka.py:134,157 /
+ *                           hf/attention.py:142
+ *   fmka_attn_decode_splitkv  the single-token decode attention
+ *                           (fastmka.py:166-174; hf/attention.py:188-193)
+ *   fmka_gemm_bf16          the output projection wo / o_proj
+ *                           (fastmka.py:175-176; hf/attention.py:194-195)
+ *   fmka_get_last_error     the TORCH_CHECK / cudaGetLastError error reporting of
+ *                           fastmka_attn.cu:134-150,169-170
+ */
+#ifndef FASTMKA_B200_H_
+#define FASTMKA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define FMKA_API __attribute__((visibility("default")))
+#else
+#define FMKA_API
+#endif
+
+typedef struct CUstream_st* fmka_stream_t; /* same handle as cudaStream_t */
+
+enum {
+  FMKA_OK = 0,
+  FMKA_ERR_INVALID_ARGUMENT = 1,
+  FMKA_ERR_UNSUPPORTED = 2,
+  FMKA_ERR_CUDA = 3,
+  FMKA_ERR_WORKSPACE = 4,
+  FMKA_ERR_DEVICE = 5
+};
+
+/* Device status bits set by kernels (see fmka_device_status). */
+enum {
+  FMKA_STATUS_WAIT_TIMEOUT = 1,     /* a pipeline wait in a kernel ran out of time */
+  FMKA_STATUS_LOOKBACK_TIMEOUT = 2, /* the EMA scan's look-back ran out of time */
+  FMKA_STATUS_BAD_LAUNCH = 4
+};
+
+/* Library version string. */
+FMKA_API const char* fmka_version(void);
+
+/* Last error of the calling thread: returns its status code and copies the
+ * NUL-terminated message into buf (truncated to buflen). */
+FMKA_API int fmka_get_last_error(char* buf, int buflen);
+
+/* Reads the current device's kernel status word into *status (after
+ * synchronising `stream`) and clears it when `clear` is nonzero. A nonzero
+ * word means some kernel gave up on a bounded wait; its outputs are invalid. */
+FMKA_API int fmka_device_status(uint32_t* status, int clear, fmka_stream_t stream);
+
+/* Number of SMs of the current device. */
+FMKA_API int fmka_num_sms(void);
+
+/* ---------------------------------------------------------------- GEMMs ---
+ * fmka_gemm_bf16: C[M, N] = A[M, K] * W[N, K]^T (+ bias[N]), bf16 in/out,
+ * fp32 accumulation (tcgen05). K, lda, ldw, ldc multiples of 8. */
+FMKA_API int fmka_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, const float* bias, void* c, int64_t ldc,
+                   int M, int N, int K, fmka_stream_t stream);
+
+/* fmka_qr_proj: one GEMM over x[M = B*T, D] with the stacked weight
+ * w_qr = [Wq ; W1 * Wq]  ([Nq + R, D]) and fp32 bias_qr ([Nq + R] or NULL).
+ *   columns [0, Nq)      -> q in head-split layout [B, Hq, T, 128] at strides
+ *                           (q_sb, q_sh, q_st), token slots from t_offset, with
+ *                           rotate-half RoPE when cos/sin are given
+ *                           (fp32 [.., T, 128] at strides (rope_sb, rope_st))
+ *   columns [Nq, Nq + R) -> router hidden h = act(. + bias), accumulated as
+ *                           logits[m, l] += sum_r w2[l, r] * h[r]
+ *                           (logits fp32 [M, L]; the caller zeroes it first)
+ * act: 0 = SiLU, 1 = GELU (erf). Nq = Hq * 128, Nq % 128 == 0. */
+FMKA_API int fmka_qr_proj(const void* x, int64_t ldx, const void* w_qr, int64_t ldw, const float* bias_qr, int B, int T,
+                 int D, int Hq, int R, void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, int t_offset,
+                 const float* rope_cos, const float* rope_sin, int64_t rope_sb, int64_t rope_st, const float* w2,
+                 int L, int act, float* logits, fmka_stream_t stream);
+
+/* fmka_kv_proj: one GEMM over h[M = B*T, D] with w_kv = [Wk ; Wv]
+ * ([2 * Hkv * 128, D]) and fp32 bias_kv ([2 * Hkv * 128] or NULL). k and v are
+ * written in head-split layout at token slots [t_offset, t_offset + T), RoPE on
+ * k when cos/sin are given. */
+FMKA_API int fmka_kv_proj(const void* h, int64_t ldh, const void* w_kv, int64_t ldw, const float* bias_kv, int B, int T,
+                 int D, int Hkv, void* k, void* v, int64_t kv_sb, int64_t kv_sh, int64_t kv_st, int t_offset,
+                 const float* rope_cos, const float* rope_sin, int64_t rope_sb, int64_t rope_st,
+                 fmka_stream_t stream);
+
+/* ------------------------------------------------- stage 1: route + EMA ---
+ * lam = softmax(logits + b2) (or `gate` given directly), L2 = causal prefix EMA
+ * of x with decay beta (zero initial state), H = lam0*x + lam1*L2 (+ lam2*L3).
+ * L3 row for token t is min(t, T3 - 1) (the reference's repeat / truncate /
+ * pad-with-last-row rule); l3_st may be 0 to broadcast one row. Exactly one of
+ * logits / gate is non-NULL. lam (fp32 [B, T, L]) may be NULL. */
+FMKA_API size_t fmka_route_ema_blend_workspace_size(int B, int T, int D);
+FMKA_API int fmka_route_ema_blend(const void* x, int64_t x_sb, int64_t x_st, const float* logits, const float* b2,
+                         const float* gate, int L, const void* l3, int64_t l3_sb, int64_t l3_st, int T3, float beta,
+                         int B, int T, int D, void* h, int64_t h_sb, int64_t h_st, float* lam, void* workspace,
+                         size_t workspace_bytes, fmka_stream_t stream);
+
+/* Route blend with all three memories given (no scan):
+ * H = gate0*l1 + gate1*l2 (+ gate2*l3), gate fp32 [B*T, L]. This is the blend
+ * inside the reference's fused route kernel (mka/cuda/fused_route_mka.cu:60-67,
+ * reached through fused_route_mka_attn, mka/cuda/ops.py:47-70). */
+FMKA_API int fmka_route_blend(const void* l1, int64_t l1_sb, int64_t l1_st, const void* l2, int64_t l2_sb, int64_t l2_st,
+                     const void* l3, int64_t l3_sb, int64_t l3_st, int T3, const float* gate, int L, int B, int T,
+                     int D, void* h, int64_t h_sb, int64_t h_st, fmka_stream_t stream);
+
+/* ------------------------------------------------------------ attention ---
+ * Prefill: o[b, t, hq, :] = softmax(scale * q k^T + causal mask) v, with GQA
+ * (kv head = hq / (Hq / Hkv)) and bottom-right causal alignment (query t sees
+ * keys <= t + Tk - Tq). lse[b, hq, t] (natural log of the scaled scores) may be
+ * NULL. head_dim must be 128. */
+FMKA_API int fmka_attn_fwd_prefill(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, const void* k, const void* v,
+                          int64_t kv_sb, int64_t kv_sh, int64_t kv_st, void* o, int64_t o_sb, int64_t o_st,
+                          int64_t o_sh, float* lse, int64_t lse_sb, int64_t lse_sh, int B, int Hq, int Hkv, int Tq,
+                          int Tk, int head_dim, int causal, float scale, fmka_stream_t stream);
+
+/* Decode: one query token per sequence against Tk cached keys.
+ * q[b, hq, :] at (q_sb, q_sh); o[b, hq, :] at (o_sb, o_sh); lse[b, hq] may be
+ * NULL. num_splits <= 0 picks a split count for the device; the workspace size
+ * depends on it. At most 16 query heads per kv head. */
+FMKA_API int fmka_attn_decode_num_splits(int B, int Hkv, int Tk);
+FMKA_API size_t fmka_attn_decode_workspace_size(int B, int Hq, int Hkv, int Tk, int num_splits);
+FMKA_API int fmka_attn_decode_splitkv(const void* q, int64_t q_sb, int64_t q_sh, const void* k, const void* v, int64_t kv_sb,
+                             int64_t kv_sh, int64_t kv_st, void* o, int64_t o_sb, int64_t o_sh, float* lse,
+                             int64_t lse_sb, int B, int Hq, int Hkv, int Tk, int head_dim, float scale,
+                             int num_splits, void* workspace, size_t workspace_bytes, fmka_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FASTMKA_B200_H_ */

@@ -1,0 +1,346 @@
+// C-ABI entry points of libfastmka_b200.so (declared in include/fastmka_b200.h):
+// argument checking, the per-thread error channel, the per-device kernel status
+// word, TMA tensor-map encoding, and the GEMM epilogue wiring for the Q/router
+// and K/V projections.
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/fastmka_b200.h"
+#include "fmka_internal.h"
+
+namespace fmka {
+
+// Implemented in the kernel translation units.
+size_t route_ema_blend_workspace_bytes(int B, int T, int D);
+int launch_route_ema_blend(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, const __nv_bfloat16* l2,
+                           int64_t l2_sb, int64_t l2_st, const float* logits,
+                           const float* b2, const float* gate, int L, const __nv_bfloat16* l3, int64_t l3_sb,
+                           int64_t l3_st, int T3, float beta, int B, int T, int D, __nv_bfloat16* h,
+                           int64_t h_sb, int64_t h_st, float* lam, void* workspace, size_t workspace_bytes,
+                           bool clear_flags, cudaStream_t stream);
+int launch_attn_prefill(const __nv_bfloat16* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
+                        const __nv_bfloat16* k, const __nv_bfloat16* v, int64_t kv_sb, int64_t kv_sh,
+                        int64_t kv_st, __nv_bfloat16* o, int64_t o_sb, int64_t o_st, int64_t o_sh, float* lse,
+                        int64_t lse_sb, int64_t lse_sh, int B, int Hq, int Hkv, int Tq, int Tk, int head_dim,
+                        int causal, float scale, cudaStream_t stream);
+size_t attn_decode_workspace_bytes(int B, int Hq, int num_splits);
+int attn_decode_plan(int B, int Hkv, int Tk, int requested, int* keys_per_split_out);
+int launch_attn_decode(const __nv_bfloat16* q, int64_t q_sb, int64_t q_sh, const __nv_bfloat16* k,
+                       const __nv_bfloat16* v, int64_t kv_sb, int64_t kv_sh, int64_t kv_st, __nv_bfloat16* o,
+                       int64_t o_sb, int64_t o_sh, float* lse, int64_t lse_sb, int B, int Hq, int Hkv, int Tk,
+                       int head_dim, float scale, int num_splits, void* workspace, size_t workspace_bytes,
+                       cudaStream_t stream);
+
+// ----------------------------------------------------------------- errors --
+namespace {
+thread_local int g_last_code = 0;
+thread_local char g_last_msg[512] = {0};
+}  // namespace
+
+int set_error(int code, const std::string& msg) {
+  g_last_code = code;
+  std::snprintf(g_last_msg, sizeof(g_last_msg), "%s", msg.c_str());
+  return code;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return kOk;
+  return set_error(kErrCuda, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// ------------------------------------------------------- per-device state --
+namespace {
+constexpr int kMaxDevices = 64;
+__device__ uint32_t g_status_word;  // OR of FMKA_STATUS_* bits
+uint32_t* g_status_ptr[kMaxDevices] = {nullptr};
+int g_num_sms[kMaxDevices] = {0};
+std::mutex g_dev_mu;
+
+int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  return dev;
+}
+}  // namespace
+
+uint32_t* device_status_word() {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  if (g_status_ptr[dev] != nullptr) return g_status_ptr[dev];
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (g_status_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status_word) == cudaSuccess) g_status_ptr[dev] = static_cast<uint32_t*>(p);
+  }
+  return g_status_ptr[dev];
+}
+
+int num_sms_current_device() {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  if (g_num_sms[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    g_num_sms[dev] = n;
+  }
+  return g_num_sms[dev];
+}
+
+// ------------------------------------------------------------ tensor maps --
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+}  // namespace
+
+int make_tmap_bf16(CUtensorMap* out, const void* base, int rank, const uint64_t* dims,
+                   const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128) {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (g_encode == nullptr) return set_error(kErrCuda, "cuTensorMapEncodeTiled is unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    return set_error(kErrInvalidArgument, "TMA base address must be 16-byte aligned");
+  cuuint64_t gdim[5];
+  cuuint64_t gstride[4];
+  cuuint32_t bdim[5];
+  cuuint32_t estr[5];
+  for (int i = 0; i < rank; ++i) {
+    gdim[i] = dims[i];
+    bdim[i] = box[i];
+    estr[i] = 1;
+    if (i > 0) {
+      gstride[i - 1] = strides_bytes[i - 1];
+      if (strides_bytes[i - 1] % 16 != 0)
+        return set_error(kErrInvalidArgument, "TMA strides must be multiples of 16 bytes");
+    }
+  }
+  CUresult r = g_encode(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), gdim, gstride, bdim,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(kErrCuda, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
+  return kOk;
+}
+
+}  // namespace fmka
+
+using namespace fmka;
+
+namespace {
+inline cudaStream_t as_stream(fmka_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+inline const __nv_bfloat16* bf(const void* p) { return static_cast<const __nv_bfloat16*>(p); }
+inline __nv_bfloat16* bfw(void* p) { return static_cast<__nv_bfloat16*>(p); }
+
+GemmSeg empty_seg() {
+  GemmSeg s;
+  std::memset(&s, 0, sizeof(s));
+  return s;
+}
+}  // namespace
+
+extern "C" {
+
+const char* fmka_version(void) { return "fastmka_b200 0.1.0 (sm_100a)"; }
+
+int fmka_get_last_error(char* buf, int buflen) {
+  if (buf != nullptr && buflen > 0) std::snprintf(buf, (size_t)buflen, "%s", g_last_msg);
+  return g_last_code;
+}
+
+int fmka_device_status(uint32_t* status, int clear, fmka_stream_t stream) {
+  uint32_t* dev = device_status_word();
+  if (dev == nullptr) return set_error(kErrDevice, "device status word unavailable");
+  uint32_t host = 0;
+  int rc = check_cuda(cudaMemcpyAsync(&host, dev, sizeof(host), cudaMemcpyDeviceToHost, as_stream(stream)),
+                      "status read");
+  if (rc) return rc;
+  rc = check_cuda(cudaStreamSynchronize(as_stream(stream)), "status sync");
+  if (rc) return rc;
+  if (clear) {
+    rc = check_cuda(cudaMemsetAsync(dev, 0, sizeof(uint32_t), as_stream(stream)), "status clear");
+    if (rc) return rc;
+  }
+  if (status) *status = host;
+  return kOk;
+}
+
+int fmka_num_sms(void) { return num_sms_current_device(); }
+
+int fmka_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, const float* bias, void* c, int64_t ldc,
+                   int M, int N, int K, fmka_stream_t stream) {
+  if (a == nullptr || w == nullptr || c == nullptr) return set_error(kErrInvalidArgument, "gemm: null pointer");
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.n_split = N;
+  p.seg[0] = empty_seg();
+  p.seg[0].kind = kSegRowMajor;
+  p.seg[0].n_begin = 0;
+  p.seg[0].n_end = N;
+  p.seg[0].out = bfw(c);
+  p.seg[0].ld = ldc;
+  p.seg[0].bias = bias;
+  p.seg[1] = empty_seg();
+  p.status = device_status_word();
+  return launch_gemm(bf(a), lda, bf(w), ldw, p, num_sms_current_device(), as_stream(stream));
+}
+
+int fmka_qr_proj(const void* x, int64_t ldx, const void* w_qr, int64_t ldw, const float* bias_qr, int B, int T,
+                 int D, int Hq, int R, void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, int t_offset,
+                 const float* rope_cos, const float* rope_sin, int64_t rope_sb, int64_t rope_st, const float* w2,
+                 int L, int act, float* logits, fmka_stream_t stream) {
+  if (x == nullptr || w_qr == nullptr || q == nullptr) return set_error(kErrInvalidArgument, "qr_proj: null pointer");
+  if (B <= 0 || T <= 0 || D <= 0 || Hq <= 0 || R < 0) return set_error(kErrInvalidArgument, "qr_proj: bad shape");
+  if ((rope_cos == nullptr) != (rope_sin == nullptr))
+    return set_error(kErrInvalidArgument, "qr_proj: pass both rope cos and sin or neither");
+  if (act != 0 && act != 1) return set_error(kErrInvalidArgument, "qr_proj: act must be 0 (SiLU) or 1 (GELU)");
+  if ((q_sb % 8) || (q_sh % 8) || (q_st % 8)) return set_error(kErrInvalidArgument, "qr_proj: q strides % 8");
+  const int Nq = Hq * 128;
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = B * T;
+  p.N = Nq + R;
+  p.K = D;
+  p.n_split = Nq;
+  p.seg[0] = empty_seg();
+  p.seg[0].kind = kSegHeads;
+  p.seg[0].n_begin = 0;
+  p.seg[0].n_end = Nq;
+  p.seg[0].out = bfw(q);
+  p.seg[0].bias = bias_qr;
+  p.seg[0].T = T;
+  p.seg[0].head_dim = 128;
+  p.seg[0].s_b = q_sb;
+  p.seg[0].s_h = q_sh;
+  p.seg[0].s_t = q_st;
+  p.seg[0].t_offset = t_offset;
+  p.seg[0].rope_cos = rope_cos;
+  p.seg[0].rope_sin = rope_sin;
+  p.seg[0].rope_sb = rope_sb;
+  p.seg[0].rope_st = rope_st;
+  p.seg[1] = empty_seg();
+  if (R > 0) {
+    if (w2 == nullptr || logits == nullptr || L < 1 || L > 4)
+      return set_error(kErrInvalidArgument, "qr_proj: router needs w2, logits and 1..4 levels");
+    p.seg[1].kind = kSegRouter;
+    p.seg[1].n_begin = Nq;
+    p.seg[1].n_end = Nq + R;
+    p.seg[1].bias = bias_qr ? bias_qr + Nq : nullptr;
+    p.seg[1].w2 = w2;
+    p.seg[1].L = L;
+    p.seg[1].act = act;
+    p.seg[1].logits = logits;
+  }
+  p.status = device_status_word();
+  return launch_gemm(bf(x), ldx, bf(w_qr), ldw, p, num_sms_current_device(), as_stream(stream));
+}
+
+int fmka_kv_proj(const void* h, int64_t ldh, const void* w_kv, int64_t ldw, const float* bias_kv, int B, int T,
+                 int D, int Hkv, void* k, void* v, int64_t kv_sb, int64_t kv_sh, int64_t kv_st, int t_offset,
+                 const float* rope_cos, const float* rope_sin, int64_t rope_sb, int64_t rope_st,
+                 fmka_stream_t stream) {
+  if (h == nullptr || w_kv == nullptr || k == nullptr || v == nullptr)
+    return set_error(kErrInvalidArgument, "kv_proj: null pointer");
+  if (B <= 0 || T <= 0 || D <= 0 || Hkv <= 0) return set_error(kErrInvalidArgument, "kv_proj: bad shape");
+  if ((rope_cos == nullptr) != (rope_sin == nullptr))
+    return set_error(kErrInvalidArgument, "kv_proj: pass both rope cos and sin or neither");
+  if ((kv_sb % 8) || (kv_sh % 8) || (kv_st % 8)) return set_error(kErrInvalidArgument, "kv_proj: kv strides % 8");
+  const int Nk = Hkv * 128;
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = B * T;
+  p.N = 2 * Nk;
+  p.K = D;
+  p.n_split = Nk;
+  for (int s = 0; s < 2; ++s) {
+    p.seg[s] = empty_seg();
+    p.seg[s].kind = kSegHeads;
+    p.seg[s].n_begin = s * Nk;
+    p.seg[s].n_end = (s + 1) * Nk;
+    p.seg[s].out = bfw(s == 0 ? k : v);
+    p.seg[s].bias = bias_kv ? bias_kv + s * Nk : nullptr;
+    p.seg[s].T = T;
+    p.seg[s].head_dim = 128;
+    p.seg[s].s_b = kv_sb;
+    p.seg[s].s_h = kv_sh;
+    p.seg[s].s_t = kv_st;
+    p.seg[s].t_offset = t_offset;
+  }
+  p.seg[0].rope_cos = rope_cos;
+  p.seg[0].rope_sin = rope_sin;
+  p.seg[0].rope_sb = rope_sb;
+  p.seg[0].rope_st = rope_st;
+  p.status = device_status_word();
+  return launch_gemm(bf(h), ldh, bf(w_kv), ldw, p, num_sms_current_device(), as_stream(stream));
+}
+
+size_t fmka_route_ema_blend_workspace_size(int B, int T, int D) {
+  if (B <= 0 || T <= 0 || D <= 0) return 0;
+  return route_ema_blend_workspace_bytes(B, T, D);
+}
+
+int fmka_route_ema_blend(const void* x, int64_t x_sb, int64_t x_st, const float* logits, const float* b2,
+                         const float* gate, int L, const void* l3, int64_t l3_sb, int64_t l3_st, int T3, float beta,
+                         int B, int T, int D, void* h, int64_t h_sb, int64_t h_st, float* lam, void* workspace,
+                         size_t workspace_bytes, fmka_stream_t stream) {
+  if (x == nullptr || h == nullptr) return set_error(kErrInvalidArgument, "route_ema_blend: null pointer");
+  if (!std::isfinite(beta)) return set_error(kErrInvalidArgument, "route_ema_blend: beta must be finite");
+  return launch_route_ema_blend(bf(x), x_sb, x_st, nullptr, 0, 0, logits, b2, gate, L, bf(l3), l3_sb, l3_st, T3,
+                                beta, B, T, D, bfw(h), h_sb, h_st, lam, workspace, workspace_bytes, true,
+                                as_stream(stream));
+}
+
+int fmka_route_blend(const void* l1, int64_t l1_sb, int64_t l1_st, const void* l2, int64_t l2_sb, int64_t l2_st,
+                     const void* l3, int64_t l3_sb, int64_t l3_st, int T3, const float* gate, int L, int B, int T,
+                     int D, void* h, int64_t h_sb, int64_t h_st, fmka_stream_t stream) {
+  if (l1 == nullptr || l2 == nullptr || gate == nullptr || h == nullptr)
+    return set_error(kErrInvalidArgument, "route_blend: null pointer");
+  return launch_route_ema_blend(bf(l1), l1_sb, l1_st, bf(l2), l2_sb, l2_st, nullptr, nullptr, gate, L, bf(l3), l3_sb,
+                                l3_st, T3, 0.f, B, T, D, bfw(h), h_sb, h_st, nullptr, nullptr, 0, false,
+                                as_stream(stream));
+}
+
+int fmka_attn_fwd_prefill(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, const void* k, const void* v,
+                          int64_t kv_sb, int64_t kv_sh, int64_t kv_st, void* o, int64_t o_sb, int64_t o_st,
+                          int64_t o_sh, float* lse, int64_t lse_sb, int64_t lse_sh, int B, int Hq, int Hkv, int Tq,
+                          int Tk, int head_dim, int causal, float scale, fmka_stream_t stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr)
+    return set_error(kErrInvalidArgument, "attn_prefill: null pointer");
+  return launch_attn_prefill(bf(q), q_sb, q_sh, q_st, bf(k), bf(v), kv_sb, kv_sh, kv_st, bfw(o), o_sb, o_st, o_sh,
+                             lse, lse_sb, lse_sh, B, Hq, Hkv, Tq, Tk, head_dim, causal, scale, as_stream(stream));
+}
+
+int fmka_attn_decode_num_splits(int B, int Hkv, int Tk) {
+  if (B <= 0 || Hkv <= 0 || Tk <= 0) return 1;
+  return attn_decode_plan(B, Hkv, Tk, 0, nullptr);
+}
+
+size_t fmka_attn_decode_workspace_size(int B, int Hq, int Hkv, int Tk, int num_splits) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Tk <= 0) return 0;
+  const int s = attn_decode_plan(B, Hkv, Tk, num_splits, nullptr);
+  return attn_decode_workspace_bytes(B, Hq, s);
+}
+
+int fmka_attn_decode_splitkv(const void* q, int64_t q_sb, int64_t q_sh, const void* k, const void* v, int64_t kv_sb,
+                             int64_t kv_sh, int64_t kv_st, void* o, int64_t o_sb, int64_t o_sh, float* lse,
+                             int64_t lse_sb, int B, int Hq, int Hkv, int Tk, int head_dim, float scale,
+                             int num_splits, void* workspace, size_t workspace_bytes, fmka_stream_t stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr)
+    return set_error(kErrInvalidArgument, "attn_decode: null pointer");
+  return launch_attn_decode(bf(q), q_sb, q_sh, bf(k), bf(v), kv_sb, kv_sh, kv_st, bfw(o), o_sb, o_sh, lse, lse_sb,
+                            B, Hq, Hkv, Tk, head_dim, scale, num_splits, workspace, workspace_bytes,
+                            as_stream(stream));
+}
+
+}  // extern "C"

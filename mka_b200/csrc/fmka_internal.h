@@ -1,0 +1,77 @@
+// Internal declarations shared by the FastMKA CUDA translation units: launch
+// parameter structs, kernel launchers and the per-thread error channel that the
+// C-ABI entry points report through.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace fmka {
+
+// ----------------------------------------------------------------- errors --
+// Status codes returned by every C-ABI entry point (0 = success).
+enum Status : int {
+  kOk = 0,
+  kErrInvalidArgument = 1,
+  kErrUnsupported = 2,
+  kErrCuda = 3,
+  kErrWorkspace = 4,
+  kErrDevice = 5,
+};
+
+// Records `msg` as this thread's last error and returns `code`.
+int set_error(int code, const std::string& msg);
+// Checks a CUDA runtime result; on failure records it and returns kErrCuda.
+int check_cuda(cudaError_t e, const char* what);
+
+// ------------------------------------------------------------- tensor maps --
+// Encodes a rank-2 or rank-3 bf16 tiled tensor map with 128-byte swizzle.
+// dims/strides are innermost first; strides are in bytes for dims 1..rank-1.
+int make_tmap_bf16(CUtensorMap* out, const void* base, int rank, const uint64_t* dims,
+                   const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128);
+
+// ------------------------------------------------------------------- GEMM --
+enum SegKind : int { kSegRowMajor = 0, kSegHeads = 1, kSegRouter = 2 };
+
+struct GemmSeg {
+  int kind;
+  int n_begin;           // first global column of this segment
+  int n_end;             // one past the last column of this segment
+  __nv_bfloat16* out;    // row-major: [M, ld]; heads: [B, H, Tcap, Dh] through strides
+  int64_t ld;            // row-major row stride (elements)
+  const float* bias;     // indexed by (n - n_begin); may be null
+  int T;                 // tokens per batch row (rows m = b*T + t)
+  int head_dim;          // 128
+  int64_t s_b, s_h, s_t; // element strides of the head-split output
+  int t_offset;          // first token slot written in the head-split output
+  const float* rope_cos; // [*, T, head_dim] fp32 or null (no RoPE)
+  const float* rope_sin;
+  int64_t rope_sb, rope_st;
+  const float* w2;       // router second layer [L, R] fp32
+  int L;
+  int act;               // 0 = SiLU, 1 = GELU (erf)
+  float* logits;         // [M, L] fp32, accumulated
+};
+
+struct GemmParams {
+  int M, N, K;
+  int n_split;  // columns < n_split use seg[0], the rest seg[1]
+  GemmSeg seg[2];
+  uint32_t* status;
+};
+
+// C = A[M,K] * B[N,K]^T with the segment epilogues. A and B are row-major bf16
+// with row strides lda / ldb (elements).
+int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int64_t ldb, const GemmParams& p,
+                int num_sms, cudaStream_t stream);
+
+// Device status word used by kernels to report bounded-wait timeouts; one per
+// device, allocated lazily.
+uint32_t* device_status_word();
+int num_sms_current_device();
+
+}  // namespace fmka

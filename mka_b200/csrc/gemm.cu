@@ -1,0 +1,387 @@
+// Persistent tcgen05 GEMM for the FastMKA projections:
+//   C[M, N] = A[M, K] * B[N, K]^T        (A = activations, B = nn.Linear weight)
+//
+// One CTA per SM walks the output tiles (BM = 128 rows x BN columns). Warp roles:
+//   warp 0      TMA producer: A/B K-slices (64 bf16 = one 128-byte swizzle row)
+//               into a STAGES-deep shared-memory ring
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=BN, K=16)
+//               into a double-buffered fp32 accumulator in TMEM
+//   warp 2      TMEM allocator
+//   warps 4..7  epilogue: tcgen05.ld of the accumulator rows (thread i <-> row i),
+//               then one of three fused epilogues:
+//                 row-major     bias + bf16 store
+//                 heads         bias + optional rotate-half RoPE + store straight
+//                               into the [B, H, T, Dh] head-split layout
+//                 router        bias + SiLU/GELU + dot with the router's second
+//                               layer, accumulated into per-token gate logits
+// The accumulator is double-buffered so the epilogue of tile i overlaps the
+// main loop of tile i+1.
+//
+// Replaces the nn.Linear calls of the reference FastMKA forward
+// (mka/layers/fastmka.py:79,91,98-99,176; mka/hf/attention.py:95,104,110-111,195).
+#include "fmka_internal.h"
+#include "ptx.cuh"
+
+namespace fmka {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreads = 256;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kABytes = kBM * kBK * 2;  // 16 KB
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ float act_fn(float v, int act) {
+  if (act == 0) return v / (1.0f + __expf(-v));             // SiLU
+  return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));  // GELU (erf form)
+}
+
+// Stores 32 fp32 values (already final) as bf16 to dst (16-byte aligned when
+// all 32 are in range); `nvalid` limits the columns written.
+__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float* v, int nvalid) {
+  if (nvalid >= 32 && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w;
+      w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+      w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+      w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+      w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+      d4[q] = w;
+    }
+  } else {
+    for (int j = 0; j < nvalid && j < 32; ++j) dst[j] = __float2bfloat16_rn(v[j]);
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * Cfg::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tfull = bars + 2 * S;
+  uint64_t* tempty = bars + 2 * S + 2;
+  uint64_t* mma_done = bars + 2 * S + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  const int num_m = (p.M + kBM - 1) / kBM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (p.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer --
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long issued = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        const int m0 = (tile / num_n) * kBM;
+        const int n0 = (tile % num_n) * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          tma_load_2d(sA + stage * Cfg::kABytes, &tmA, &full[stage], kb * kBK, m0);
+          tma_load_2d(sB + stage * Cfg::kBBytes, &tmB, &full[stage], kb * kBK, n0);
+          ++issued;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain: make sure no TMA write is still landing in shared memory when
+      // the CTA tears down (they have all completed on the normal path).
+      const long pending = issued < S ? issued : S;
+      for (long i = 0; i < pending; ++i) {
+        if (--stage < 0) {
+          stage = S - 1;
+          phase ^= 1u;
+        }
+        mbar_wait(&full[stage], phase, p.status);
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA --
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t aphase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], aphase ^ 1u, p.status)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * Cfg::kABytes);
+          const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            umma_ss(d_tmem, desc_kmajor_sw128(a_addr + k * 32), desc_kmajor_sw128(b_addr + k * 32), idesc,
+                    (kb | k) != 0);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_commit(&tfull[acc]);
+      }
+      // All MMAs issued by this thread complete before teardown.
+      tc_commit(mma_done);
+      mbar_wait(mma_done, 0, p.status);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue --
+    const int ew = warp - 4;
+    const int row_in_tile = ew * 32 + lane;
+    const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(ew * 32) << 16);
+    int it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t aphase = (it >> 1) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aphase, p.status))) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int m0 = (tile / num_n) * kBM;
+      const int n0 = (tile % num_n) * BN;
+      const int m = m0 + row_in_tile;
+      const bool row_ok = m < p.M;
+      const GemmSeg& sg = (n0 >= p.n_split) ? p.seg[1] : p.seg[0];
+      const uint32_t acc_addr = lane_addr + acc * BN;
+
+      if (sg.kind == kSegRowMajor) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(acc_addr + c * 32, r);
+          tmem_wait_ld();
+          const int n = n0 + c * 32;
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float b = 0.f;
+            if (sg.bias != nullptr && n + j < sg.n_end) b = __ldg(sg.bias + (n + j - sg.n_begin));
+            v[j] = __uint_as_float(r[j]) + b;
+          }
+          if (row_ok && n < sg.n_end) {
+            store_row32(sg.out + (int64_t)m * sg.ld + (n - sg.n_begin), v, sg.n_end - n);
+          }
+        }
+      } else if (sg.kind == kSegHeads) {
+        const int b = row_ok ? m / sg.T : 0;
+        const int t = row_ok ? m % sg.T : 0;
+        const int hd = sg.head_dim;  // 128
+        const bool rope = sg.rope_cos != nullptr;
+        const float* cs = rope ? sg.rope_cos + (int64_t)b * sg.rope_sb + (int64_t)t * sg.rope_st : nullptr;
+        const float* sn = rope ? sg.rope_sin + (int64_t)b * sg.rope_sb + (int64_t)t * sg.rope_st : nullptr;
+#pragma unroll 1
+        for (int hh = 0; hh < BN / 128; ++hh) {
+          const int nl_head = n0 - sg.n_begin + hh * 128;  // first column of this head in the segment
+          const int head = nl_head / hd;
+#pragma unroll 1
+          for (int c2 = 0; c2 < 2; ++c2) {
+            uint32_t r1[32], r2[32];
+            tmem_ld32(acc_addr + hh * 128 + c2 * 32, r1);
+            tmem_ld32(acc_addr + hh * 128 + 64 + c2 * 32, r2);
+            tmem_wait_ld();
+            const bool in_range = (n0 + hh * 128) < sg.n_end;
+            float o1[32], o2[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int d1 = c2 * 32 + j;
+              const int d2 = d1 + 64;
+              float x1 = __uint_as_float(r1[j]);
+              float x2 = __uint_as_float(r2[j]);
+              if (sg.bias != nullptr && in_range) {
+                x1 += __ldg(sg.bias + nl_head + d1);
+                x2 += __ldg(sg.bias + nl_head + d2);
+              }
+              if (rope && row_ok) {
+                o1[j] = x1 * __ldg(cs + d1) - x2 * __ldg(sn + d1);
+                o2[j] = x2 * __ldg(cs + d2) + x1 * __ldg(sn + d2);
+              } else {
+                o1[j] = x1;
+                o2[j] = x2;
+              }
+            }
+            if (row_ok && in_range) {
+              __nv_bfloat16* dst =
+                  sg.out + (int64_t)b * sg.s_b + (int64_t)head * sg.s_h + (int64_t)(t + sg.t_offset) * sg.s_t;
+              store_row32(dst + c2 * 32, o1, 32);
+              store_row32(dst + 64 + c2 * 32, o2, 32);
+            }
+          }
+        }
+      } else {  // kSegRouter
+        float part[4] = {0.f, 0.f, 0.f, 0.f};
+        const int R = sg.n_end - sg.n_begin;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(acc_addr + c * 32, r);
+          tmem_wait_ld();
+          const int nl = n0 - sg.n_begin + c * 32;
+#pragma unroll 4
+          for (int j = 0; j < 32; ++j) {
+            if (nl + j < R) {
+              float v = __uint_as_float(r[j]);
+              if (sg.bias != nullptr) v += __ldg(sg.bias + nl + j);
+              const float a = act_fn(v, sg.act);
+#pragma unroll
+              for (int l = 0; l < 4; ++l)
+                if (l < sg.L) part[l] += __ldg(sg.w2 + (int64_t)l * R + nl + j) * a;
+            }
+          }
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int l = 0; l < 4; ++l)
+            if (l < sg.L) atomicAdd(sg.logits + (int64_t)m * sg.L + l, part[l]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace
+
+int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int64_t ldb, const GemmParams& p,
+                int num_sms, cudaStream_t stream) {
+  if (p.M <= 0 || p.N <= 0 || p.K <= 0) return set_error(kErrInvalidArgument, "gemm: M, N, K must be positive");
+  if (p.K % 8 != 0 || lda % 8 != 0 || ldb % 8 != 0)
+    return set_error(kErrInvalidArgument, "gemm: K and row strides must be multiples of 8 elements");
+  if ((reinterpret_cast<uintptr_t>(A) & 15u) || (reinterpret_cast<uintptr_t>(B) & 15u))
+    return set_error(kErrInvalidArgument, "gemm: A and B must be 16-byte aligned");
+
+  // Tile width: 256 when every segment boundary is 256-aligned, else 128.
+  int BN = 256;
+  if (p.n_split % 256 != 0 && p.n_split < p.N) BN = 128;
+  if (p.n_split % 128 != 0 && p.n_split < p.N)
+    return set_error(kErrInvalidArgument, "gemm: segment split must be a multiple of 128 columns");
+  for (int s = 0; s < 2; ++s) {
+    const GemmSeg& g = p.seg[s];
+    if (g.n_end <= g.n_begin) continue;
+    if (g.kind == kSegHeads && (g.head_dim != 128 || (g.n_end - g.n_begin) % 128 != 0 || g.T <= 0))
+      return set_error(kErrUnsupported, "gemm: head-split epilogue needs head_dim 128 and whole heads");
+    if (g.kind == kSegRouter && (g.L < 1 || g.L > 4 || g.w2 == nullptr || g.logits == nullptr))
+      return set_error(kErrInvalidArgument, "gemm: router epilogue needs 1..4 levels, w2 and logits");
+    if (g.kind == kSegRowMajor && (g.ld % 8 != 0))
+      return set_error(kErrInvalidArgument, "gemm: output row stride must be a multiple of 8");
+  }
+
+  CUtensorMap tmA, tmB;
+  {
+    uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.M};
+    uint64_t strides[1] = {(uint64_t)lda * 2};
+    uint32_t box[2] = {kBK, kBM};
+    int rc = make_tmap_bf16(&tmA, A, 2, dims, strides, box, true);
+    if (rc) return rc;
+  }
+  {
+    uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.N};
+    uint64_t strides[1] = {(uint64_t)ldb * 2};
+    uint32_t box[2] = {kBK, (uint32_t)BN};
+    int rc = make_tmap_bf16(&tmB, B, 2, dims, strides, box, true);
+    if (rc) return rc;
+  }
+
+  const int num_tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN);
+  const int grid = num_tiles < num_sms ? num_tiles : num_sms;
+  if (BN == 256) {
+    auto k = gemm_tcgen05_kernel<256>;
+    const int smem = GemmCfg<256>::kSmemBytes;
+    int rc = check_cuda(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), "gemm attr");
+    if (rc) return rc;
+    k<<<grid, kThreads, smem, stream>>>(tmA, tmB, p);
+  } else {
+    auto k = gemm_tcgen05_kernel<128>;
+    const int smem = GemmCfg<128>::kSmemBytes;
+    int rc = check_cuda(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), "gemm attr");
+    if (rc) return rc;
+    k<<<grid, kThreads, smem, stream>>>(tmA, tmB, p);
+  }
+  return check_cuda(cudaGetLastError(), "gemm launch");
+}
+
+}  // namespace fmka

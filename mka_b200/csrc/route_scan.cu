@@ -1,0 +1,397 @@
+// Stage 1 of the FastMKA forward: routing gate + causal prefix EMA + route blend.
+//
+//   lam[b,t,:] = softmax(logits[b,t,:] + b2)                  (router output)
+//   L2[b,t,:]  = beta * L2[b,t-1,:] + (1 - beta) * X[b,t,:],  L2[b,-1,:] = 0
+//   H[b,t,:]   = lam0 * X + lam1 * L2 (+ lam2 * L3[b, min(t, T3-1), :])
+//
+// Reference: causal_prefix_ema (mka/layers/session_memory.py:6-22),
+// repeat_retrieval_to_length (session_memory.py:25-39), gate and blend
+// (mka/layers/fastmka.py:91-96, mka/hf/attention.py:104-107). The reference
+// runs the EMA as a Python loop of T steps (about 4T kernel launches); here the
+// whole stage is one single-pass kernel that reads X (and L3) once and writes H
+// once.
+//
+// Parallel scan. The EMA is a linear recurrence, so the state after a chunk is
+// the chunk's zero-state scan ("aggregate") plus beta^len times the state that
+// entered it; a chunk only needs its incoming state S_in to finish. Each CTA owns (batch row,
+// 256-channel slice, 64-token chunk). Eight warps each scan eight tokens with
+// 128-bit loads (lane = 8 channels); warp aggregates are combined in shared
+// memory; the chunk's incoming state comes from a decoupled look-back over
+// preceding chunks of the same (batch, slice): each CTA publishes its chunk
+// aggregate, then walks back over published aggregates until it finds a
+// published inclusive state. Chunk order comes from an atomic ticket, so a CTA
+// only ever waits on CTAs that started before it. Waits are bounded; a timeout
+// sets a status bit and the scan continues with a zero contribution.
+#include "fmka_internal.h"
+#include "ptx.cuh"
+
+namespace fmka {
+
+namespace {
+
+constexpr int kChunkT = 64;   // tokens per CTA
+constexpr int kSlice = 256;   // channels per CTA (32 lanes x 8)
+constexpr int kWarps = 8;
+constexpr int kTokPerWarp = kChunkT / kWarps;  // 8
+constexpr int kThreads = kWarps * 32;
+
+constexpr uint32_t kFlagAgg = 1;
+constexpr uint32_t kFlagInc = 2;
+
+struct ScanParams {
+  const __nv_bfloat16* x;  // [B, T, D]
+  int64_t x_sb, x_st;
+  const float* logits;     // [B*T, L] router logits without the output bias
+  const float* b2;         // [L] or null
+  const float* gate;       // alternatively: precomputed gate [B*T, L] (logits == null)
+  int L;
+  const __nv_bfloat16* l2; // given L2 [B, T, D] (blend only, no scan) or null
+  int64_t l2_sb, l2_st;
+  const __nv_bfloat16* l3; // [B, T3, D] or null
+  int64_t l3_sb, l3_st;
+  int T3;
+  float beta, one_minus_beta, beta8, beta64;
+  int B, T, D;
+  __nv_bfloat16* h;        // [B, T, D]
+  int64_t h_sb, h_st;
+  float* lam;              // [B, T, L] or null
+  uint32_t* ticket;
+  uint32_t* flags;         // [nseq * nchunks]
+  float* agg;              // [nseq * nchunks * kSlice]
+  float* inc;              // [nseq * nchunks * kSlice]
+  int nds, nchunks;
+  uint32_t* status;
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  f[0] = bf16lo_to_f32(u.x);
+  f[1] = bf16hi_to_f32(u.x);
+  f[2] = bf16lo_to_f32(u.y);
+  f[3] = bf16hi_to_f32(u.y);
+  f[4] = bf16lo_to_f32(u.z);
+  f[5] = bf16hi_to_f32(u.z);
+  f[6] = bf16lo_to_f32(u.w);
+  f[7] = bf16hi_to_f32(u.w);
+}
+
+__global__ void __launch_bounds__(kThreads, 2) route_ema_blend_kernel(const __grid_constant__ ScanParams p) {
+  __shared__ uint32_t s_tile;
+  __shared__ float s_wagg[kWarps][kSlice];
+  __shared__ float s_in[kSlice];
+  __shared__ float s_lam[kChunkT][4];
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  const bool scan = p.l2 == nullptr;  // grid-uniform
+  if (threadIdx.x == 0) s_tile = scan ? atomicAdd(p.ticket, 1u) : blockIdx.x;
+  __syncthreads();
+  const int tile = static_cast<int>(s_tile);
+  const int nseq = p.B * p.nds;
+  const int chunk = tile / nseq;
+  const int seq = tile % nseq;
+  const int b = seq / p.nds;
+  const int ds = seq % p.nds;
+  const int t0 = chunk * kChunkT;
+  const int d0 = ds * kSlice + lane * 8;
+  const bool ch_ok = d0 < p.D;
+
+  // ---- gate for the chunk's tokens ----
+  if (threadIdx.x < kChunkT) {
+    const int t = t0 + threadIdx.x;
+    float g[4] = {0.f, 0.f, 0.f, 0.f};
+    if (t < p.T) {
+      const int64_t row = (int64_t)b * p.T + t;
+      if (p.logits != nullptr) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+          if (l < p.L) {
+            g[l] = p.logits[row * p.L + l] + (p.b2 ? p.b2[l] : 0.f);
+            mx = fmaxf(mx, g[l]);
+          }
+        }
+        float sum = 0.f;
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+          if (l < p.L) {
+            g[l] = __expf(g[l] - mx);
+            sum += g[l];
+          }
+        }
+        const float inv = 1.f / sum;
+#pragma unroll
+        for (int l = 0; l < 4; ++l) g[l] *= inv;
+      } else {
+#pragma unroll
+        for (int l = 0; l < 4; ++l)
+          if (l < p.L) g[l] = p.gate[row * p.L + l];
+      }
+      if (p.lam != nullptr && ds == 0) {
+#pragma unroll
+        for (int l = 0; l < 4; ++l)
+          if (l < p.L) p.lam[row * p.L + l] = g[l];
+      }
+    }
+#pragma unroll
+    for (int l = 0; l < 4; ++l) s_lam[threadIdx.x][l] = g[l];
+  }
+
+  // ---- load this warp's 8 tokens x 8 channels (128-bit loads) ----
+  const int tw = t0 + warp * kTokPerWarp;
+  uint4 xr[kTokPerWarp];
+#pragma unroll
+  for (int i = 0; i < kTokPerWarp; ++i) {
+    const int t = tw + i;
+    if (ch_ok && t < p.T) {
+      xr[i] = __ldcs(reinterpret_cast<const uint4*>(p.x + (int64_t)b * p.x_sb + (int64_t)t * p.x_st + d0));
+    } else {
+      xr[i] = make_uint4(0, 0, 0, 0);
+    }
+  }
+
+  // ---- local scan from a zero state: only the warp aggregate is kept; the
+  // output pass re-runs the recurrence from the true incoming state ----
+  if (scan) {
+    float st[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < kTokPerWarp; ++i) {
+      float xf[8];
+      unpack8(xr[i], xf);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) st[c] = p.beta * st[c] + p.one_minus_beta * xf[c];
+    }
+#pragma unroll
+    for (int c = 0; c < 8; ++c) s_wagg[warp][lane * 8 + c] = st[c];
+  }
+  __syncthreads();
+
+  // ---- chunk aggregate + decoupled look-back (warp 0) ----
+  if (scan && warp == 0) {
+    float a[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) v = p.beta8 * v + s_wagg[w][lane * 8 + c];
+      a[c] = v;
+    }
+    const int64_t rec = (int64_t)seq * p.nchunks + chunk;
+    float sin_[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (chunk == 0) {
+      float4* dst = reinterpret_cast<float4*>(p.inc + rec * kSlice + lane * 8);
+      __stcg(dst, make_float4(a[0], a[1], a[2], a[3]));
+      __stcg(dst + 1, make_float4(a[4], a[5], a[6], a[7]));
+      __threadfence();
+      __syncwarp();
+      if (lane == 0) st_release_u32(p.flags + rec, kFlagInc);
+    } else {
+      {
+        float4* dst = reinterpret_cast<float4*>(p.agg + rec * kSlice + lane * 8);
+        __stcg(dst, make_float4(a[0], a[1], a[2], a[3]));
+        __stcg(dst + 1, make_float4(a[4], a[5], a[6], a[7]));
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) st_release_u32(p.flags + rec, kFlagAgg);
+      }
+      float mult = 1.f;
+      for (int pc = chunk - 1; pc >= 0; --pc) {
+        const int64_t prec = (int64_t)seq * p.nchunks + pc;
+        uint32_t f = 0;
+        if (lane == 0) {
+          f = ld_acquire_u32(p.flags + prec);
+          if (f == 0) {
+            const uint64_t tstart = globaltimer_ns();
+            while ((f = ld_acquire_u32(p.flags + prec)) == 0) {
+              __nanosleep(64);
+              if (globaltimer_ns() - tstart > kWaitLimitNs) {
+                atomicOr(p.status, kStatusLookbackTimeout);
+                f = 0xFFFFFFFFu;
+                break;
+              }
+            }
+          }
+        }
+        f = __shfl_sync(0xffffffffu, f, 0);
+        if (f == 0xFFFFFFFFu) break;  // timed out: treat the rest as zero
+        (void)ld_acquire_u32(p.flags + prec);  // per-lane acquire before reading the record
+        const float* src = (f == kFlagInc ? p.inc : p.agg) + prec * kSlice + lane * 8;
+        const float4 v0 = __ldcg(reinterpret_cast<const float4*>(src));
+        const float4 v1 = __ldcg(reinterpret_cast<const float4*>(src) + 1);
+        sin_[0] += mult * v0.x;
+        sin_[1] += mult * v0.y;
+        sin_[2] += mult * v0.z;
+        sin_[3] += mult * v0.w;
+        sin_[4] += mult * v1.x;
+        sin_[5] += mult * v1.y;
+        sin_[6] += mult * v1.z;
+        sin_[7] += mult * v1.w;
+        if (f == kFlagInc) break;
+        mult *= p.beta64;
+      }
+      float inc[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) inc[c] = a[c] + p.beta64 * sin_[c];
+      float4* dst = reinterpret_cast<float4*>(p.inc + rec * kSlice + lane * 8);
+      __stcg(dst, make_float4(inc[0], inc[1], inc[2], inc[3]));
+      __stcg(dst + 1, make_float4(inc[4], inc[5], inc[6], inc[7]));
+      __threadfence();
+      __syncwarp();
+      if (lane == 0) st_release_u32(p.flags + rec, kFlagInc);
+    }
+#pragma unroll
+    for (int c = 0; c < 8; ++c) s_in[lane * 8 + c] = sin_[c];
+  }
+  __syncthreads();
+
+  // ---- state entering this warp's tokens ----
+  float st[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (scan) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      float v = s_in[lane * 8 + c];
+      for (int w = 0; w < warp; ++w) v = p.beta8 * v + s_wagg[w][lane * 8 + c];
+      st[c] = v;
+    }
+  }
+
+  // ---- blend and store ----
+#pragma unroll
+  for (int i = 0; i < kTokPerWarp; ++i) {
+    const int t = tw + i;
+    const int tl = warp * kTokPerWarp + i;
+    const float g0 = s_lam[tl][0], g1 = s_lam[tl][1], g2 = s_lam[tl][2];
+    float xf[8];
+    unpack8(xr[i], xf);
+    float l3f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (p.l3 != nullptr && ch_ok && t < p.T) {
+      const int t3 = t < p.T3 ? t : p.T3 - 1;
+      const uint4 u = __ldcs(reinterpret_cast<const uint4*>(p.l3 + (int64_t)b * p.l3_sb + (int64_t)t3 * p.l3_st + d0));
+      unpack8(u, l3f);
+    }
+    float l2f[8];
+    if (!scan && ch_ok && t < p.T) {
+      const uint4 u = __ldcs(reinterpret_cast<const uint4*>(p.l2 + (int64_t)b * p.l2_sb + (int64_t)t * p.l2_st + d0));
+      unpack8(u, l2f);
+    }
+    float o[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      if (scan) {
+        st[c] = p.beta * st[c] + p.one_minus_beta * xf[c];  // L2 at token t
+      } else {
+        st[c] = (ch_ok && t < p.T) ? l2f[c] : 0.f;
+      }
+      float v = g0 * xf[c] + g1 * st[c];
+      if (p.l3 != nullptr) v += g2 * l3f[c];
+      o[c] = v;
+    }
+    if (ch_ok && t < p.T) {
+      uint4 w;
+      w.x = pack_bf16x2(o[0], o[1]);
+      w.y = pack_bf16x2(o[2], o[3]);
+      w.z = pack_bf16x2(o[4], o[5]);
+      w.w = pack_bf16x2(o[6], o[7]);
+      __stcs(reinterpret_cast<uint4*>(p.h + (int64_t)b * p.h_sb + (int64_t)t * p.h_st + d0), w);
+    }
+  }
+}
+
+}  // namespace
+
+size_t route_ema_blend_workspace_bytes(int B, int T, int D) {
+  const int64_t nds = (D + kSlice - 1) / kSlice;
+  const int64_t nchunks = (T + kChunkT - 1) / kChunkT;
+  const int64_t nrec = (int64_t)B * nds * nchunks;
+  const int64_t flag_bytes = ((nrec * 4 + 256 + 255) / 256) * 256;  // ticket + flags, 256-aligned
+  return (size_t)(flag_bytes + 2 * nrec * kSlice * 4);
+}
+
+size_t route_ema_blend_flag_bytes(int B, int T, int D) {
+  const int64_t nds = (D + kSlice - 1) / kSlice;
+  const int64_t nchunks = (T + kChunkT - 1) / kChunkT;
+  const int64_t nrec = (int64_t)B * nds * nchunks;
+  return (size_t)(((nrec * 4 + 256 + 255) / 256) * 256);
+}
+
+int launch_route_ema_blend(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, const __nv_bfloat16* l2,
+                           int64_t l2_sb, int64_t l2_st, const float* logits,
+                           const float* b2, const float* gate, int L, const __nv_bfloat16* l3, int64_t l3_sb,
+                           int64_t l3_st, int T3, float beta, int B, int T, int D, __nv_bfloat16* h,
+                           int64_t h_sb, int64_t h_st, float* lam, void* workspace, size_t workspace_bytes,
+                           bool clear_flags, cudaStream_t stream) {
+  if (B <= 0 || T <= 0 || D <= 0) return set_error(kErrInvalidArgument, "route_ema_blend: empty shape");
+  if (D % 8 != 0) return set_error(kErrUnsupported, "route_ema_blend: d_model must be a multiple of 8");
+  if (L < 2 || L > 3) return set_error(kErrInvalidArgument, "route_ema_blend: levels must be 2 or 3");
+  if (L == 3 && (l3 == nullptr || T3 < 1))
+    return set_error(kErrInvalidArgument, "route_ema_blend: 3 levels need an L3 memory with >= 1 row");
+  if ((logits == nullptr) == (gate == nullptr))
+    return set_error(kErrInvalidArgument, "route_ema_blend: pass exactly one of logits or gate");
+  if ((x_st % 8) || (x_sb % 8) || (h_st % 8) || (h_sb % 8) || (l3 && ((l3_st % 8) || (l3_sb % 8))) ||
+      (l2 && ((l2_st % 8) || (l2_sb % 8))))
+    return set_error(kErrInvalidArgument, "route_ema_blend: strides must be multiples of 8 elements");
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) || (reinterpret_cast<uintptr_t>(h) & 15u) ||
+      (l3 && (reinterpret_cast<uintptr_t>(l3) & 15u)) || (l2 && (reinterpret_cast<uintptr_t>(l2) & 15u)))
+    return set_error(kErrInvalidArgument, "route_ema_blend: tensors must be 16-byte aligned");
+  const size_t need = route_ema_blend_workspace_bytes(B, T, D);
+  if (l2 == nullptr && (workspace == nullptr || workspace_bytes < need))
+    return set_error(kErrWorkspace, "route_ema_blend: workspace too small (need " + std::to_string(need) + " bytes)");
+  if (l2 == nullptr && (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return set_error(kErrInvalidArgument, "route_ema_blend: workspace must be 256-byte aligned");
+
+  ScanParams p;
+  p.x = x;
+  p.x_sb = x_sb;
+  p.x_st = x_st;
+  p.l2 = l2;
+  p.l2_sb = l2_sb;
+  p.l2_st = l2_st;
+  p.logits = logits;
+  p.b2 = b2;
+  p.gate = gate;
+  p.L = L;
+  p.l3 = (L == 3) ? l3 : nullptr;
+  p.l3_sb = l3_sb;
+  p.l3_st = l3_st;
+  p.T3 = T3;
+  p.beta = beta;
+  p.one_minus_beta = 1.0f - beta;
+  p.beta8 = (float)__builtin_powi((double)beta, 8);
+  p.beta64 = (float)__builtin_powi((double)beta, 64);
+  p.B = B;
+  p.T = T;
+  p.D = D;
+  p.h = h;
+  p.h_sb = h_sb;
+  p.h_st = h_st;
+  p.lam = lam;
+  p.nds = (D + kSlice - 1) / kSlice;
+  p.nchunks = (T + kChunkT - 1) / kChunkT;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const size_t flag_bytes = route_ema_blend_flag_bytes(B, T, D);
+  const int64_t nrec = (int64_t)B * p.nds * p.nchunks;
+  p.ticket = reinterpret_cast<uint32_t*>(ws);
+  p.flags = reinterpret_cast<uint32_t*>(ws + 256);
+  p.agg = reinterpret_cast<float*>(ws + flag_bytes);
+  p.inc = p.agg + nrec * kSlice;
+  p.status = device_status_word();
+  if (clear_flags && l2 == nullptr) {
+    int rc = check_cuda(cudaMemsetAsync(ws, 0, flag_bytes, stream), "route_ema_blend memset");
+    if (rc) return rc;
+  }
+  const int64_t grid = nrec;
+  if (grid > 0x7FFFFFFF) return set_error(kErrUnsupported, "route_ema_blend: problem too large");
+  route_ema_blend_kernel<<<(unsigned)grid, kThreads, 0, stream>>>(p);
+  return check_cuda(cudaGetLastError(), "route_ema_blend launch");
+}
+
+}  // namespace fmka

@@ -1,0 +1,350 @@
+"""Tensor-level FastMKA ops on B200, each one call into libfastmka_b200.so.
+
+Every op launches on the current torch CUDA stream of its inputs' device, takes
+bf16 CUDA tensors (the reference-compatible wrappers at the bottom also accept
+fp16/fp32 and convert), allocates its outputs with torch, and raises
+FastMKAError / RuntimeError on bad input. There is no CPU path: calling an op
+with CPU tensors raises.
+
+Reference op API mirrored here: mka/cuda/ops.py (fastmka_attn :73-77,
+fused_route_mka_attn :47-70, has_fastmka_cuda :25-26, has_fused_route_mka_cuda
+:43-44).
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+HEAD_DIM = 128
+ACT_SILU = 0
+ACT_GELU = 1
+
+
+# ------------------------------------------------------------------ helpers --
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _check_cuda(*ts: Optional[torch.Tensor]) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("FastMKA B200 ops need CUDA tensors (there is no CPU fallback)")
+
+
+def _check_bf16(*ts: Optional[torch.Tensor]) -> None:
+    for t in ts:
+        if t is not None and t.dtype != torch.bfloat16:
+            raise RuntimeError(f"expected a bfloat16 tensor, got {t.dtype}")
+
+
+def _f32(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+    if t is None:
+        return None
+    return t.detach().to(torch.float32).contiguous()
+
+
+class _Workspace:
+    """Grow-only per-(device, stream) scratch buffer; reuse is stream-ordered."""
+
+    def __init__(self) -> None:
+        self._bufs: dict[tuple[int, int], torch.Tensor] = {}
+
+    def get(self, device: torch.device, nbytes: int) -> Optional[torch.Tensor]:
+        if nbytes <= 0:
+            return None
+        key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+        buf = self._bufs.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            self._bufs[key] = buf
+        return buf
+
+
+_WS = _Workspace()
+
+
+def device_status(clear: bool = True) -> int:
+    """Returns (and by default clears) the device status word of the current device."""
+    st = _lib.c_uint32(0)
+    _lib.call("fmka_device_status", _lib.ctypes.byref(st), int(clear), torch.cuda.current_stream().cuda_stream)
+    return int(st.value)
+
+
+# -------------------------------------------------------------------- GEMMs --
+def gemm(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
+         out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[M, N] = a[M, K] @ w[N, K]^T (+ bias), bf16 with fp32 accumulation."""
+    _check_cuda(a, w)
+    _check_bf16(a, w)
+    if a.dim() != 2 or w.dim() != 2 or a.shape[1] != w.shape[1]:
+        raise RuntimeError("gemm: expected a [M, K] and w [N, K]")
+    if a.stride(1) != 1 or w.stride(1) != 1:
+        raise RuntimeError("gemm: inner dimension must be contiguous")
+    M, K = a.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    b32 = _f32(bias)
+    _lib.call("fmka_gemm_bf16", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), _ptr(b32),
+              out.data_ptr(), out.stride(0), M, N, K, _stream(a))
+    return out
+
+
+def qr_proj(x2d: torch.Tensor, w_qr: torch.Tensor, bias_qr: Optional[torch.Tensor], B: int, T: int,
+            num_heads: int, router_hidden: int, w2: Optional[torch.Tensor], levels: int, act: int,
+            rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+            q_out: Optional[torch.Tensor] = None, t_offset: int = 0) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Q projection (head-split, optional RoPE) fused with the router's first layer.
+
+    Returns q [B, Hq, T, 128] and router logits [B*T, L] (fp32, without the
+    router's output bias), or None for the logits when router_hidden == 0.
+    """
+    _check_cuda(x2d, w_qr)
+    _check_bf16(x2d, w_qr)
+    D = x2d.shape[1]
+    if q_out is None:
+        q_out = torch.empty((B, num_heads, T, HEAD_DIM), dtype=torch.bfloat16, device=x2d.device)
+    logits = None
+    if router_hidden > 0:
+        logits = torch.zeros((B * T, levels), dtype=torch.float32, device=x2d.device)
+    cos, sin, rsb, rst = _rope_args(rope, B, T)
+    w2c = _f32(w2)
+    _lib.call("fmka_qr_proj", x2d.data_ptr(), x2d.stride(0), w_qr.data_ptr(), w_qr.stride(0), _ptr(bias_qr),
+              B, T, D, num_heads, router_hidden, q_out.data_ptr(), q_out.stride(0), q_out.stride(1),
+              q_out.stride(2), t_offset, _ptr(cos), _ptr(sin), rsb, rst, _ptr(w2c), levels, act, _ptr(logits),
+              _stream(x2d))
+    return q_out, logits
+
+
+def kv_proj(h2d: torch.Tensor, w_kv: torch.Tensor, bias_kv: Optional[torch.Tensor], B: int, T: int,
+            num_kv_heads: int, rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+            k_out: Optional[torch.Tensor] = None, v_out: Optional[torch.Tensor] = None,
+            t_offset: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
+    """K/V projection of the fused memory, written head-split ([B, Hkv, Tcap, 128])."""
+    _check_cuda(h2d, w_kv)
+    _check_bf16(h2d, w_kv)
+    D = h2d.shape[1]
+    if k_out is None:
+        k_out = torch.empty((B, num_kv_heads, T, HEAD_DIM), dtype=torch.bfloat16, device=h2d.device)
+    if v_out is None:
+        v_out = torch.empty_like(k_out)
+    if k_out.stride() != v_out.stride():
+        raise RuntimeError("kv_proj: k and v outputs must share strides")
+    cos, sin, rsb, rst = _rope_args(rope, B, T)
+    _lib.call("fmka_kv_proj", h2d.data_ptr(), h2d.stride(0), w_kv.data_ptr(), w_kv.stride(0), _ptr(bias_kv),
+              B, T, D, num_kv_heads, k_out.data_ptr(), v_out.data_ptr(), k_out.stride(0), k_out.stride(1),
+              k_out.stride(2), t_offset, _ptr(cos), _ptr(sin), rsb, rst, _stream(h2d))
+    return k_out, v_out
+
+
+def _rope_args(rope, B: int, T: int):
+    """Normalises (cos, sin) of shape [T, 128], [1|B, T, 128] or [1|B, 1, T, 128] to fp32."""
+    if rope is None:
+        return None, None, 0, 0
+    cos, sin = rope
+    out = []
+    for t in (cos, sin):
+        t = t.detach()
+        if t.dim() == 4:
+            t = t[:, 0]
+        if t.dim() == 2:
+            t = t.unsqueeze(0)
+        if t.shape[-1] != HEAD_DIM or t.shape[-2] != T or t.shape[0] not in (1, B):
+            raise RuntimeError(f"rope cos/sin must be [1|B, T, 128], got {tuple(t.shape)}")
+        out.append(t.to(torch.float32).contiguous())
+    cos, sin = out
+    sb = 0 if cos.shape[0] == 1 else cos.stride(0)
+    return cos, sin, sb, cos.stride(1)
+
+
+# ----------------------------------------------------------------- stage 1 --
+def route_ema_blend(x: torch.Tensor, beta: float, logits: Optional[torch.Tensor] = None,
+                    b2: Optional[torch.Tensor] = None, gate: Optional[torch.Tensor] = None,
+                    levels: int = 2, l3: Optional[torch.Tensor] = None,
+                    want_lam: bool = True) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """H = lam0 * x + lam1 * EMA(x) (+ lam2 * L3) with lam = softmax(logits + b2) (or `gate`).
+
+    x [B, T, D] bf16 (token rows contiguous in D); l3 [B, T3, D] bf16 or None.
+    Returns H [B, T, D] bf16 and lam [B, T, L] fp32.
+    """
+    _check_cuda(x, logits, gate, l3)
+    _check_bf16(x, l3)
+    B, T, D = x.shape
+    if x.stride(2) != 1:
+        x = x.contiguous()
+    h = torch.empty((B, T, D), dtype=torch.bfloat16, device=x.device)
+    lam = torch.empty((B, T, levels), dtype=torch.float32, device=x.device) if want_lam else None
+    l3_sb = l3_st = 0
+    T3 = 0
+    if levels == 3:
+        if l3 is None:
+            raise RuntimeError("route_ema_blend: three levels need an L3 memory")
+        if l3.stride(2) != 1:
+            l3 = l3.contiguous()
+        T3 = l3.shape[1]
+        l3_sb, l3_st = l3.stride(0), (l3.stride(1) if T3 > 1 else 0)
+    ws_bytes = _lib.load().fmka_route_ema_blend_workspace_size(B, T, D)
+    ws = _WS.get(x.device, ws_bytes)
+    b2c = _f32(b2)
+    logits_c = None if logits is None else logits.contiguous()
+    gate_c = None if gate is None else gate.to(torch.float32).contiguous()
+    _lib.call("fmka_route_ema_blend", x.data_ptr(), x.stride(0), x.stride(1), _ptr(logits_c), _ptr(b2c),
+              _ptr(gate_c), levels, _ptr(l3), l3_sb, l3_st, T3, float(beta), B, T, D, h.data_ptr(),
+              h.stride(0), h.stride(1), _ptr(lam), _ptr(ws), ws_bytes, _stream(x))
+    return h, lam
+
+
+def causal_prefix_ema(x: torch.Tensor, beta: float = 0.9) -> torch.Tensor:
+    """L2[t] = beta * L2[t-1] + (1 - beta) * x[t] with L2[-1] = 0 (session_memory.py:6-22).
+
+    Runs the stage-1 kernel with the gate fixed to (0, 1), so H == EMA(x).
+    """
+    B, T, _ = x.shape
+    gate = torch.zeros((B * T, 2), dtype=torch.float32, device=x.device)
+    gate[:, 1] = 1.0
+    h, _ = route_ema_blend(x, beta, gate=gate, levels=2, want_lam=False)
+    return h
+
+
+# --------------------------------------------------------------- attention --
+def attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
+                 scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
+                 want_lse: bool = True) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Causal (bottom-right aligned) GQA attention on tcgen05.
+
+    q [B, Hq, Tq, 128], k/v [B, Hkv, Tk, 128] (any strides with contiguous head
+    dim). Returns o [B, Tq, Hq, 128] (or into `out`, any [B, Tq, Hq, 128]-indexable
+    strided view) and lse [B, Hq, Tq] fp32.
+    """
+    _check_cuda(q, k, v)
+    _check_bf16(q, k, v)
+    B, Hq, Tq, Dh = q.shape
+    _, Hkv, Tk, _ = k.shape
+    if k.stride() != v.stride() or k.shape != v.shape:
+        raise RuntimeError("attn_prefill: k and v must have the same shape and strides")
+    if scale is None:
+        scale = 1.0 / math.sqrt(Dh)
+    if out is None:
+        out = torch.empty((B, Tq, Hq, Dh), dtype=torch.bfloat16, device=q.device)
+    lse = torch.empty((B, Hq, Tq), dtype=torch.float32, device=q.device) if want_lse else None
+    _lib.call("fmka_attn_fwd_prefill", q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), k.data_ptr(),
+              v.data_ptr(), k.stride(0), k.stride(1), k.stride(2), out.data_ptr(), out.stride(0), out.stride(1),
+              out.stride(2), _ptr(lse), lse.stride(0) if lse is not None else 0,
+              lse.stride(1) if lse is not None else 0, B, Hq, Hkv, Tq, Tk, Dh, int(causal), float(scale),
+              _stream(q))
+    return out, lse
+
+
+def attn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Optional[float] = None,
+                num_splits: int = 0, out: Optional[torch.Tensor] = None,
+                want_lse: bool = True) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Single-token decode attention over Tk cached keys (split along the keys).
+
+    q [B, Hq, 1, 128] or [B, Hq, 128]; k/v [B, Hkv, Tk, 128] (strided views of a
+    larger cache are fine). Returns o [B, 1, Hq, 128] and lse [B, Hq].
+    """
+    _check_cuda(q, k, v)
+    _check_bf16(q, k, v)
+    if q.dim() == 4:
+        if q.shape[2] != 1:
+            raise RuntimeError("attn_decode: one query token per sequence")
+        q3 = q[:, :, 0]
+    else:
+        q3 = q
+    B, Hq, Dh = q3.shape
+    _, Hkv, Tk, _ = k.shape
+    if k.stride() != v.stride() or k.shape != v.shape:
+        raise RuntimeError("attn_decode: k and v must have the same shape and strides")
+    if q3.stride(2) != 1:
+        q3 = q3.contiguous()
+    if scale is None:
+        scale = 1.0 / math.sqrt(Dh)
+    if out is None:
+        out = torch.empty((B, 1, Hq, Dh), dtype=torch.bfloat16, device=q.device)
+    lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device) if want_lse else None
+    lib = _lib.load()
+    ws_bytes = lib.fmka_attn_decode_workspace_size(B, Hq, Hkv, Tk, num_splits)
+    ws = _WS.get(q.device, ws_bytes)
+    _lib.call("fmka_attn_decode_splitkv", q3.data_ptr(), q3.stride(0), q3.stride(1), k.data_ptr(), v.data_ptr(),
+              k.stride(0), k.stride(1), k.stride(2), out.data_ptr(), out.stride(0), out.stride(2), _ptr(lse),
+              lse.stride(0) if lse is not None else 0, B, Hq, Hkv, Tk, Dh, float(scale), num_splits, _ptr(ws),
+              ws_bytes, _stream(q))
+    return out, lse
+
+
+# ---------------------------------------- reference-compatible op wrappers --
+def has_fastmka_cuda() -> bool:
+    """True when the library loads and a CUDA device is visible (mka/cuda/ops.py:25-26)."""
+    try:
+        _lib.load()
+    except Exception:
+        return False
+    return torch.cuda.is_available()
+
+
+def has_fused_route_mka_cuda() -> bool:
+    """Same probe for the fused route op (mka/cuda/ops.py:43-44)."""
+    return has_fastmka_cuda()
+
+
+def _to_bf16(t: torch.Tensor) -> torch.Tensor:
+    return t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16)
+
+
+def fastmka_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True) -> torch.Tensor:
+    """Drop-in for mka.cuda.ops.fastmka_attn (ops.py:73-77): causal attention with
+    offset Tk - Tq, output [B, H, Tq, D] in q's dtype. Adds GQA and bf16; D == 128."""
+    _check_cuda(q, k, v)
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise RuntimeError("q/k/v must be 4D")
+    if q.size(0) != k.size(0) or k.shape != v.shape or q.size(3) != k.size(3):
+        raise RuntimeError("B/H mismatch or head dim mismatch")
+    if q.size(1) % k.size(1) != 0:
+        raise RuntimeError("B/H mismatch")
+    if q.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+        raise RuntimeError(f"unsupported dtype {q.dtype}")
+    qb, kb, vb = _to_bf16(q), _to_bf16(k), _to_bf16(v)
+    B, H, Tq, D = q.shape
+    out = torch.empty((B, H, Tq, D), dtype=torch.bfloat16, device=q.device)
+    if Tq == 1 and causal:
+        attn_decode(qb, kb, vb, out=out.permute(0, 2, 1, 3), want_lse=False)
+    else:
+        attn_prefill(qb, kb, vb, causal=causal, out=out.permute(0, 2, 1, 3), want_lse=False)
+    return out if q.dtype == torch.bfloat16 else out.to(q.dtype)
+
+
+def fused_route_mka_attn(q: torch.Tensor, l1: torch.Tensor, l2: torch.Tensor, l3: torch.Tensor,
+                         lam: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor) -> torch.Tensor:
+    """Drop-in for mka.cuda.ops.fused_route_mka_attn (ops.py:47-70): fused = sum_l lam_l * l_l,
+    k = fused wk^T, v = fused wv^T, causal attention with q. MHA (H * Dh == D), no cache."""
+    _check_cuda(q, l1, l2, l3, lam, wk, wv)
+    if q.dim() != 4:
+        raise RuntimeError("q must be [B,H,T,Dh]")
+    if l1.dim() != 3 or l2.dim() != 3 or l3.dim() != 3:
+        raise RuntimeError("l1/l2/l3 must be [B,T,D]")
+    B, H, T, Dh = q.shape
+    D = l1.shape[2]
+    L = lam.shape[2]
+    if L not in (2, 3):
+        raise RuntimeError("lam last dim must be 2 or 3")
+    if H * Dh != D or wk.shape != (D, D) or wv.shape != (D, D):
+        raise RuntimeError("expected H*Dh == D (hidden_size) and wk/wv [D,D]")
+    l1b, l2b, l3b = (_to_bf16(t).contiguous() for t in (l1, l2, l3))
+    gate = lam.reshape(B * T, L).to(torch.float32).contiguous()
+    h = torch.empty((B, T, D), dtype=torch.bfloat16, device=q.device)
+    _lib.call("fmka_route_blend", l1b.data_ptr(), l1b.stride(0), l1b.stride(1), l2b.data_ptr(), l2b.stride(0),
+              l2b.stride(1), l3b.data_ptr() if L == 3 else None, l3b.stride(0), l3b.stride(1), T, gate.data_ptr(), L,
+              B, T, D, h.data_ptr(), h.stride(0), h.stride(1), _stream(q))
+    w_kv = torch.cat([_to_bf16(wk), _to_bf16(wv)], 0).contiguous()
+    k, v = kv_proj(h.reshape(B * T, D), w_kv, None, B, T, H)
+    out = torch.empty((B, H, T, Dh), dtype=torch.bfloat16, device=q.device)
+    attn_prefill(_to_bf16(q), k, v, causal=True, out=out.permute(0, 2, 1, 3), want_lse=False)
+    return out if q.dtype == torch.bfloat16 else out.to(q.dtype)

@@ -1,0 +1,173 @@
+"""Op-level numerics of every CUDA kernel against a plain PyTorch fp32 reference
+of the same op, on small seeded shapes (edge cases included: ragged tiles, GQA,
+causal offsets, tails). Module-level parity with the reference algorithm lives
+in test_parity_gpu.py."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    a = a.float()
+    b = b.float()
+    return ((a - b).abs().max() / b.abs().max().clamp_min(1e-6)).item()
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from mka_b200 import ops as _ops
+
+    return _ops
+
+
+def _ref_attn(q, k, v, causal=True, scale=None):
+    """fp32 reference: q [B,Hq,Tq,D], k/v [B,Hkv,Tk,D]; bottom-right causal."""
+    B, Hq, Tq, D = q.shape
+    Hkv, Tk = k.shape[1], k.shape[2]
+    G = Hq // Hkv
+    scale = scale or 1.0 / math.sqrt(D)
+    kf = k.float().repeat_interleave(G, dim=1)
+    vf = v.float().repeat_interleave(G, dim=1)
+    s = torch.matmul(q.float(), kf.transpose(-1, -2)) * scale
+    if causal:
+        qi = torch.arange(Tk - Tq, Tk, device=q.device).view(Tq, 1)
+        ki = torch.arange(Tk, device=q.device).view(1, Tk)
+        s = s.masked_fill(ki > qi, float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)
+    o = torch.matmul(torch.softmax(s, dim=-1), vf)
+    return o, lse
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 384, 256), (1000, 1024, 1024), (77, 136, 3584)])
+def test_gemm_plain(ops, M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    a = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K)).bfloat16()
+    bias = torch.randn(N, device="cuda", generator=g)
+    out = ops.gemm(a, w, bias)
+    ref = a.float() @ w.float().t() + bias
+    assert _rel(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("B,T,Hq,R,rope,act", [(2, 100, 2, 64, False, 1), (1, 256, 4, 512, True, 0),
+                                                (3, 33, 2, 96, True, 1)])
+def test_qr_proj(ops, B, T, Hq, R, rope, act):
+    D = 256
+    L = 3
+    g = torch.Generator(device="cuda").manual_seed(7 + T)
+    x = torch.randn(B * T, D, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(Hq * 128 + R, D, device="cuda", generator=g) / math.sqrt(D)).bfloat16()
+    bias = torch.randn(Hq * 128 + R, device="cuda", generator=g) * 0.1
+    w2 = torch.randn(L, R, device="cuda", generator=g) / math.sqrt(R)
+    cs = None
+    if rope:
+        pos = torch.arange(T, device="cuda").float()
+        inv = 1.0 / (10000 ** (torch.arange(0, 128, 2, device="cuda").float() / 128))
+        ang = torch.cat([pos[:, None] * inv[None], pos[:, None] * inv[None]], -1)
+        cs = (ang.cos(), ang.sin())
+    q, logits = ops.qr_proj(x, w, bias, B, T, Hq, R, w2, L, act, rope=cs)
+    full = x.float() @ w.float().t() + bias
+    qf = full[:, : Hq * 128].view(B, T, Hq, 128).transpose(1, 2)
+    if rope:
+        cos, sin = cs
+        rot = torch.cat([-qf[..., 64:], qf[..., :64]], -1)
+        qf = qf * cos + rot * sin
+    hid = full[:, Hq * 128:]
+    hid = torch.nn.functional.silu(hid) if act == 0 else torch.nn.functional.gelu(hid)
+    lg = hid @ w2.t()
+    assert _rel(q, qf) < 1e-2
+    assert _rel(logits, lg) < 1e-3
+
+
+@pytest.mark.parametrize("rope", [False, True])
+def test_kv_proj_with_offset(ops, rope):
+    B, T, D, Hkv, Tcap, off = 2, 70, 384, 2, 100, 13
+    g = torch.Generator(device="cuda").manual_seed(3)
+    h = torch.randn(B * T, D, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(2 * Hkv * 128, D, device="cuda", generator=g) / math.sqrt(D)).bfloat16()
+    bias = torch.randn(2 * Hkv * 128, device="cuda", generator=g) * 0.1
+    kc = torch.zeros(B, Hkv, Tcap, 128, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    cs = None
+    if rope:
+        ang = torch.rand(B, T, 128, device="cuda", generator=g) * 6
+        cs = (ang.cos(), ang.sin())
+    ops.kv_proj(h, w, bias, B, T, Hkv, rope=cs, k_out=kc, v_out=vc, t_offset=off)
+    full = h.float() @ w.float().t() + bias
+    kf = full[:, : Hkv * 128].view(B, T, Hkv, 128).transpose(1, 2)
+    vf = full[:, Hkv * 128:].view(B, T, Hkv, 128).transpose(1, 2)
+    if rope:
+        cos, sin = cs[0][:, None], cs[1][:, None]
+        kf = kf * cos + torch.cat([-kf[..., 64:], kf[..., :64]], -1) * sin
+    assert _rel(kc[:, :, off:off + T], kf) < 1e-2
+    assert _rel(vc[:, :, off:off + T], vf) < 1e-2
+    assert kc[:, :, :off].abs().max().item() == 0 and kc[:, :, off + T:].abs().max().item() == 0
+
+
+def _ref_ema(x, beta):
+    out = torch.zeros_like(x)
+    st = torch.zeros_like(x[:, 0])
+    for t in range(x.shape[1]):
+        st = beta * st + (1 - beta) * x[:, t]
+        out[:, t] = st
+    return out
+
+
+@pytest.mark.parametrize("B,T,D,L,T3,beta", [(2, 64, 256, 2, 0, 0.9), (2, 300, 520, 3, 1, 0.9),
+                                             (1, 1000, 1024, 3, 700, 0.99), (3, 5, 264, 3, 9, 0.5),
+                                             (1, 4100, 512, 2, 0, 0.999)])
+def test_route_ema_blend(ops, B, T, D, L, T3, beta):
+    g = torch.Generator(device="cuda").manual_seed(T + D)
+    x = torch.randn(B, T, D, device="cuda", generator=g).bfloat16()
+    logits = torch.randn(B * T, L, device="cuda", generator=g)
+    b2 = torch.randn(L, device="cuda", generator=g)
+    l3 = torch.randn(B, T3, D, device="cuda", generator=g).bfloat16() if L == 3 else None
+    h, lam = ops.route_ema_blend(x, beta, logits=logits, b2=b2, levels=L, l3=l3)
+    lam_ref = torch.softmax(logits + b2, -1).view(B, T, L)
+    ema = _ref_ema(x.float(), beta)
+    ref = lam_ref[..., 0:1] * x.float() + lam_ref[..., 1:2] * ema
+    if L == 3:
+        idx = torch.clamp(torch.arange(T, device="cuda"), max=T3 - 1)
+        ref = ref + lam_ref[..., 2:3] * l3.float()[:, idx]
+    assert ops.device_status() == 0
+    assert _rel(lam, lam_ref) < 1e-5
+    assert _rel(h, ref) < 1e-2
+
+
+def test_causal_prefix_ema_op(ops):
+    g = torch.Generator(device="cuda").manual_seed(11)
+    x = torch.randn(2, 777, 136, device="cuda", generator=g).bfloat16()
+    out = ops.causal_prefix_ema(x, 0.9)
+    assert _rel(out, _ref_ema(x.float(), 0.9)) < 1e-2
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Tq,Tk,causal", [(1, 1, 1, 128, 128, True), (2, 4, 2, 200, 200, True),
+                                                   (1, 7, 1, 300, 300, True), (2, 2, 2, 64, 333, True),
+                                                   (1, 2, 1, 130, 257, False), (1, 4, 4, 1024, 1024, True)])
+def test_attn_prefill(ops, B, Hq, Hkv, Tq, Tk, causal):
+    g = torch.Generator(device="cuda").manual_seed(Tq * 7 + Tk)
+    q = torch.randn(B, Hq, Tq, 128, device="cuda", generator=g).bfloat16()
+    k = torch.randn(B, Hkv, Tk, 128, device="cuda", generator=g).bfloat16()
+    v = torch.randn(B, Hkv, Tk, 128, device="cuda", generator=g).bfloat16()
+    o, lse = ops.attn_prefill(q, k, v, causal=causal)
+    ro, rlse = _ref_attn(q, k, v, causal)
+    assert ops.device_status() == 0
+    assert _rel(o, ro.transpose(1, 2)) < 2e-2
+    assert (lse - rlse).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Tk,splits", [(2, 4, 1, 100, 0), (3, 32, 8, 2000, 0), (1, 28, 4, 4096, 3),
+                                                (4, 8, 8, 64, 1), (2, 16, 1, 777, 0)])
+def test_attn_decode(ops, B, Hq, Hkv, Tk, splits):
+    g = torch.Generator(device="cuda").manual_seed(Tk)
+    q = torch.randn(B, Hq, 1, 128, device="cuda", generator=g).bfloat16()
+    k = torch.randn(B, Hkv, Tk, 128, device="cuda", generator=g).bfloat16()
+    v = torch.randn(B, Hkv, Tk, 128, device="cuda", generator=g).bfloat16()
+    o, lse = ops.attn_decode(q, k, v, num_splits=splits)
+    ro, rlse = _ref_attn(q, k, v, causal=True)
+    assert ops.device_status() == 0
+    assert _rel(o, ro.transpose(1, 2)) < 2e-2
+    assert (lse - rlse[..., 0]).abs().max().item() < 2e-2
