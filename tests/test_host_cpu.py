@@ -1,0 +1,149 @@
+"""CPU-only checks of the host side: the C-ABI library loads and exports every
+entry point include/fastmka_b200.h declares (no compute is launched), argument
+errors come back as status codes with messages, the Python layers keep the
+reference's API, and weight preparation is exact."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+import torch.nn as nn
+
+from tests import golden_io
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "fastmka_b200.h")
+
+
+def _header_functions():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"FMKA_API\s+[\w\s\*]+?\b(fmka_\w+)\s*\(", src)))
+
+
+def test_library_exports_every_header_symbol():
+    from mka_b200 import _lib
+
+    lib = _lib.load()
+    names = _header_functions()
+    assert len(names) >= 14
+    for n in names:
+        assert hasattr(lib, n), n
+    assert set(names) == set(_lib.exported_symbols())
+    assert b"sm_100a" in lib.fmka_version()
+
+
+def test_argument_errors_are_status_codes():
+    from mka_b200 import _lib
+
+    lib = _lib.load()
+    rc = lib.fmka_gemm_bf16(None, 0, None, 0, None, None, 0, 1, 1, 1, None)
+    assert rc == 1  # FMKA_ERR_INVALID_ARGUMENT
+    code, msg = _lib.last_error()
+    assert code == 1 and "null" in msg
+    rc = lib.fmka_attn_fwd_prefill(None, 0, 0, 0, None, None, 0, 0, 0, None, 0, 0, 0, None, 0, 0,
+                                   1, 1, 1, 1, 1, 128, 1, 1.0, None)
+    assert rc == 1
+    with pytest.raises(_lib.FastMKAError, match="null"):
+        _lib.call("fmka_route_ema_blend", None, 0, 0, None, None, None, 2, None, 0, 0, 0, 0.9, 1, 1, 8, None, 0, 0,
+                  None, None, 0, None)
+
+
+def test_workspace_sizes():
+    from mka_b200 import _lib
+
+    lib = _lib.load()
+    # route/EMA: ticket + flags (256-aligned) + two fp32 [records, 256] arrays
+    B, T, D = 4, 8192, 3584
+    nrec = B * ((D + 255) // 256) * ((T + 63) // 64)
+    flag_bytes = ((nrec * 4 + 256 + 255) // 256) * 256
+    assert lib.fmka_route_ema_blend_workspace_size(B, T, D) == flag_bytes + 2 * nrec * 256 * 4
+    assert lib.fmka_route_ema_blend_workspace_size(0, 1, 1) == 0
+    # decode with one split needs no workspace; more splits need (Dh + 1) floats per (b, h, split)
+    assert lib.fmka_attn_decode_workspace_size(2, 8, 8, 64, 1) == 0
+    assert lib.fmka_attn_decode_workspace_size(2, 8, 8, 4096, 4) == 2 * 8 * 4 * 129 * 4
+
+
+def test_ops_refuse_cpu_tensors():
+    from mka_b200 import ops
+
+    q = torch.zeros(1, 1, 128, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.attn_prefill(q, q, q)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.causal_prefix_ema(torch.zeros(1, 4, 8, dtype=torch.bfloat16))
+
+
+def test_fastmka_module_matches_reference_parameters():
+    """Same parameter names and shapes as the reference module (golden state_dict)."""
+    from mka_b200 import FastMKAAttention, FastMKAConfig
+
+    c = golden_io.load("fastmka_mha_l3_pad")
+    ref = golden_io.params(c)
+    m = FastMKAAttention(FastMKAConfig(hidden_size=256, num_heads=2, use_l3=True))
+    ours = {k: tuple(v.shape) for k, v in m.state_dict().items()}
+    assert ours == {k: tuple(v.shape) for k, v in ref.items()}
+    m.load_state_dict(ref)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m(torch.zeros(1, 4, 256))
+
+
+def test_hf_wrapper_reads_config_and_patch_walks_layers():
+    from transformers import LlamaConfig
+    from transformers.models.llama.modeling_llama import LlamaAttention
+
+    from mka_b200 import HFFastMKAAttention, HFPatchConfig, apply_hf_attention_patch, parse_patch_config
+
+    cfg = LlamaConfig(hidden_size=512, num_attention_heads=4, num_key_value_heads=1, intermediate_size=64,
+                      vocab_size=16)
+
+    class Layer(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.self_attn = LlamaAttention(cfg, layer_idx=0)
+
+    class Inner(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.layers = nn.ModuleList([Layer(), Layer(), nn.Module()])
+
+    class Model(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.model = Inner()
+
+    model = Model()
+    pc = parse_patch_config({"use_l3": True, "ema_beta": 0.8, "verbose": False})
+    assert pc == HFPatchConfig(use_l3=True, ema_beta=0.8, verbose=False)
+    assert apply_hf_attention_patch(model, pc) == 2
+    w = model.model.layers[0].self_attn
+    assert isinstance(w, HFFastMKAAttention)
+    assert (w.hidden_size, w.num_heads, w.num_key_value_heads, w.head_dim) == (512, 4, 1, 128)
+    assert w.router[2].out_features == 3 and w.router[0].out_features == 256
+    assert apply_hf_attention_patch(model, HFPatchConfig(mode="off")) == 0
+    with pytest.raises(ValueError):
+        apply_hf_attention_patch(nn.Linear(2, 2), HFPatchConfig(verbose=False))
+
+
+def test_prepared_weights_fold_router_through_q():
+    """router(q) == W2 act((W1 Wq) x + (W1 bq + b1)) + b2 exactly in fp32."""
+    from mka_b200.layers.prepared import prepare
+
+    torch.manual_seed(0)
+    D, R = 256, 64
+    wq, wk, wv, wo = (nn.Linear(D, D, bias=b) for b in (True, True, True, False))
+    router = nn.Sequential(nn.Linear(D, R), nn.GELU(), nn.Linear(R, 3))
+    W = prepare(wq, wk, wv, wo, router, torch.device("cpu"))
+    assert W.act == 1 and W.levels == 3 and W.router_hidden == R
+    x = torch.randn(5, D)
+    folded = x @ W.w_qr.float()[D:].t() + W.b_qr[D:]
+    direct = router[0](wq(x))
+    assert (folded - direct).abs().max().item() < 0.05  # bf16 rounding of the stacked weight
+    W2 = prepare(wq, wk, wv, wo, router, torch.device("cpu"), W)
+    assert W2 is W  # unchanged parameters reuse the prepared copy
+    with torch.no_grad():
+        wq.weight.add_(1.0)
+    assert prepare(wq, wk, wv, wo, router, torch.device("cpu"), W) is not W
+    router[1] = nn.Tanh()
+    with pytest.raises(NotImplementedError):
+        prepare(wq, wk, wv, wo, router, torch.device("cpu"))

@@ -1,0 +1,87 @@
+"""Pins the CPU oracle (oracle/fastmka_oracle.py) to the reference: every golden
+fixture was produced by running the FastLM/MKA modules themselves
+(tests/golden/make_golden.py); the oracle must reproduce them in fp32."""
+import pytest
+import torch
+
+from oracle import fastmka_oracle as orc
+from tests import golden_io
+
+ATOL = 2e-5
+
+
+def _close(a, b, tol=ATOL):
+    assert a.shape == b.shape, (a.shape, b.shape)
+    err = (a.float() - b.float()).abs().max().item()
+    scale = max(1.0, b.float().abs().max().item())
+    assert err <= tol * scale, f"max abs err {err}"
+
+
+def test_ema_and_repeat_rules():
+    g = golden_io.load("ema")
+    for beta in (0.9, 0.5, 0.99):
+        _close(orc.causal_prefix_ema(g["x"], beta), g[f"ema_{beta}"])
+    for tl in (7, 3, 12):
+        _close(orc.repeat_retrieval_to_length(g["mem"], tl), g[f"rep_{tl}"])
+    _close(orc.repeat_retrieval_to_length(g["mem"][:, :1], 9), g["rep_single_9"])
+
+
+def test_ema_closed_forms():
+    # unit impulse: (1 - beta) * beta^t ; constant input c: c * (1 - beta^(t+1))
+    beta = 0.9
+    x = torch.zeros(1, 20, 3)
+    x[0, 0] = 1.0
+    ref = (1 - beta) * beta ** torch.arange(20, dtype=torch.float32)
+    _close(orc.causal_prefix_ema(x, beta)[0, :, 0], ref, 1e-6)
+    c = torch.full((1, 30, 2), 2.5)
+    ref = 2.5 * (1 - beta ** (torch.arange(30, dtype=torch.float32) + 1))
+    _close(orc.causal_prefix_ema(c, beta)[0, :, 1], ref, 1e-6)
+
+
+def _act(case):
+    return "gelu" if int(case["act"]) == 1 else "silu"
+
+
+def _fastmka_params(case):
+    p = golden_io.params(case)
+    return {"wq": p["wq.weight"], "wk": p["wk.weight"], "wv": p["wv.weight"], "wo": p["wo.weight"],
+            "r1w": p["router.0.weight"], "r1b": p["router.0.bias"], "r2w": p["router.2.weight"],
+            "r2b": p["router.2.bias"]}
+
+
+@pytest.mark.parametrize("name", ["fastmka_mha_gelu", "fastmka_mha_l3_pad", "fastmka_mha_l3_single",
+                                  "fastmka_mha_cache", "fastmka_mha_decode"])
+def test_oracle_fastmka_matches_reference(name):
+    c = golden_io.load(name)
+    r = orc.fastmka_forward(c["x"], _fastmka_params(c), int(c["heads"]), bool(c["use_l3"]), float(c["beta"]),
+                            _act(c), l3_memory=c.get("l3"), kv_cache_k=c.get("past_k"), kv_cache_v=c.get("past_v"))
+    _close(r["out"], c["out"])
+    _close(r["k_tot"], c["k"])
+    _close(r["v_tot"], c["v"])
+    _close(r["lam"], c["lam"])
+    _close(r["lse"], c["lse"])
+
+
+def _hf_params(case):
+    p = golden_io.params(case)
+    out = {"wq": p["q_proj.weight"], "wk": p["k_proj.weight"], "wv": p["v_proj.weight"], "wo": p["o_proj.weight"],
+           "r1w": p["router.0.weight"], "r1b": p["router.0.bias"], "r2w": p["router.2.weight"],
+           "r2b": p["router.2.bias"]}
+    for short, name in (("bq", "q_proj.bias"), ("bk", "k_proj.bias"), ("bv", "v_proj.bias"),
+                        ("bo", "o_proj.bias")):
+        if name in p:
+            out[short] = p[name]
+    return out
+
+
+@pytest.mark.parametrize("name", ["hf_qwen_rope", "hf_qwen_decode", "hf_llama_norope"])
+def test_oracle_hf_matches_reference(name):
+    c = golden_io.load(name)
+    past = (c["past_k"], c["past_v"]) if "past_k" in c else None
+    r = orc.hf_fastmka_forward(c["x"], _hf_params(c), int(c["heads"]), int(c["kv_heads"]), bool(c["use_l3"]),
+                               float(c["beta"]), _act(c), past=past, cos=c.get("cos"), sin=c.get("sin"))
+    _close(r["out"], c["out"])
+    _close(r["k"], c["k"])
+    _close(r["v"], c["v"])
+    _close(r["lam"], c["lam"])
+    _close(r["lse"], c["lse"])
