@@ -1,0 +1,452 @@
+"""FastMKA attention-layer benchmark on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload (one step = one forward of a FastMKA attention layer):
+  prefill  Qwen-7B-like layer: batch 4 per GPU, seq 8192, d_model 3584, 28 query /
+           4 kv heads (GQA), head_dim 128, q/k/v bias, RoPE (theta 1e6), L1+L2
+           routing (EMA decay 0.9), router 3584 -> 512 -> 2 (SiLU), bf16,
+           X ~ N(0,1)/sqrt(3584), weights N(0, 0.02), seeded
+Also reported in the same line:
+  decode   Llama-3-8B-like layer: batch 64, one new token per sequence against a
+           32768-long cached fused K/V (in-place cache), d_model 4096, 32/8 heads,
+           router 4096 -> 2048 -> 2, cache ~ N(0,1)*0.1, X ~ N(0,1)
+
+value   = prefill tokens/s of the whole job (all ranks), inputs resident in HBM
+e2e     = the same through the module API with the input copied from pinned host
+          memory and the layer output copied back, every step
+roofline: the attention kernel (tensor-bound, algorithmic FLOPs 4*B*Hq*Dh*T(T+1)/2)
+          timed with CUDA events inside the timed steps against the measured
+          sustained bf16 peak; decode: the split-KV kernel's K/V bytes against the
+          measured HBM copy bandwidth
+Multi-GPU (torchrun): weak scaling by batch: every rank runs its own 4 sequences
+(units = (sequence, kv head) pairs, whole sequences per rank), no collective in
+the data path; the step time is the max over ranks.
+--impl reference: the reference's CPU algorithm (the CPU oracle restating
+FastLM/MKA's FastMKA forward op for op) on the host cores, one sequence per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+import torch.nn as nn
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PREFILL = dict(B=4, T=8192, D=3584, H=28, HKV=4, R=512, L=2, theta=1.0e6, bias=True)
+DECODE = dict(B=64, TK=32768, D=4096, H=32, HKV=8, R=2048, L=2, theta=5.0e5, bias=False)
+CPU_SAMPLE_T = 2048  # CPU sample: the first 2048 tokens of one prefill sequence
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            m = json.load(f)
+        return {"hbm": float(m["hbm_gbs"]), "bf16": float(m["bf16_tflops"]),
+                "bf16_sust": float(m["bf16_tflops_sustained"]), "src": "measured"}
+    except Exception:
+        return {"hbm": 6650.0, "bf16": 1590.0, "bf16_sust": 1400.0, "src": "fallback"}
+
+
+class _Rotary:
+    """Stands in for an HF rotary module: makes the wrapper apply RoPE."""
+
+    def __init__(self, theta):
+        self.theta = theta
+
+    def cos_sin(self, positions, device):
+        inv = 1.0 / (self.theta ** (torch.arange(0, 128, 2, device=device, dtype=torch.float32) / 128))
+        ang = positions.to(torch.float32)[:, None] * inv[None]
+        ang = torch.cat([ang, ang], -1)
+        return ang.cos()[None], ang.sin()[None]  # [1, T, 128]
+
+
+class _AttnHolder(nn.Module):
+    """A Qwen2/Llama-style attention module (q/k/v/o_proj) to wrap."""
+
+    def __init__(self, d, h, hkv, bias, theta):
+        super().__init__()
+        self.hidden_size, self.num_heads, self.num_key_value_heads = d, h, hkv
+        self.q_proj = nn.Linear(d, h * 128, bias=bias)
+        self.k_proj = nn.Linear(d, hkv * 128, bias=bias)
+        self.v_proj = nn.Linear(d, hkv * 128, bias=bias)
+        self.o_proj = nn.Linear(h * 128, d, bias=False)
+        self.rotary_emb = _Rotary(theta)
+
+
+def build_layer(cfg, device, seed=0):
+    from mka_b200 import HFFastMKAAttention
+
+    torch.manual_seed(seed)
+    holder = _AttnHolder(cfg["D"], cfg["H"], cfg["HKV"], cfg["bias"], cfg["theta"])
+    layer = HFFastMKAAttention(holder, use_l3=cfg["L"] == 3, ema_beta=0.9)
+    layer.router = nn.Sequential(nn.Linear(cfg["D"], cfg["R"]), nn.SiLU(), nn.Linear(cfg["R"], cfg["L"]))
+    g = torch.Generator(device=device).manual_seed(seed)
+    layer = layer.to(device=device, dtype=torch.bfloat16)
+    with torch.no_grad():
+        for m in layer.modules():
+            if isinstance(m, nn.Linear):
+                m.weight.copy_(torch.randn(m.weight.shape, generator=g, device=device) * 0.02)
+                if m.bias is not None:
+                    m.bias.copy_(torch.randn(m.bias.shape, generator=g, device=device) * 0.02)
+    return layer.eval()
+
+
+class ClockSampler:
+    """nvidia-smi SM clocks and throttle reasons sampled during a timed region."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, device_index):
+        self.idx = device_index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{device_index}.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        loaded = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        return dist, dist.get_rank(), ws, local
+    return None, 0, 1, 0
+
+
+def _barrier(dist):
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def _max_over_ranks(dist, v):
+    if dist is None:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _timed(dist, fn, steps):
+    _barrier(dist)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        fn()
+    b.record()
+    _barrier(dist)
+    return _max_over_ranks(dist, a.elapsed_time(b) / steps)
+
+
+def _stage_times(fn, steps):
+    """Average duration (ms) of each forward stage over `steps` instrumented calls."""
+    acc = {}
+    for _ in range(steps):
+        timers = []
+        fn(timers)
+        torch.cuda.synchronize()
+        for name, s, e in timers:
+            acc.setdefault(name, []).append(s.elapsed_time(e))
+    return {k: sum(v) / len(v) for k, v in acc.items()}
+
+
+def _traffic(name):
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary (profiles/)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get(name)
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------------ prefill --
+def bench_prefill(args, dist, rank, world, device, peaks):
+    from mka_b200.layers.forward import fastmka_forward
+
+    c = PREFILL
+    B, T, D = c["B"], c["T"], c["D"]
+    layer = build_layer(c, device)
+    g = torch.Generator(device=device).manual_seed(1000 + rank)
+    x = (torch.randn(B, T, D, generator=g, device=device) / math.sqrt(D)).to(torch.bfloat16)
+    cos, sin = layer.rotary_emb.cos_sin(torch.arange(T, device=device), device)
+    pe = (cos, sin)
+
+    def step():
+        layer(x, position_embeddings=pe)
+
+    for _ in range(args.warmup):
+        step()
+    ms = _timed(dist, step, args.steps)
+
+    # per-kernel times inside the same kind of step (instrumented)
+    W = layer.prepared(device)
+    st = _stage_times(lambda timers: fastmka_forward(x, W, c["H"], c["HKV"], 0.9, False, rope=pe, timers=timers),
+                      max(3, min(args.steps, 10)))
+    attn_ms = st.get("attention", float("nan"))
+    flops = 4.0 * B * c["H"] * 128 * T * (T + 1) / 2
+    achieved = flops / (attn_ms * 1e-3) / 1e12
+
+    # end to end through the module with host buffers
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty((B, T, D), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        out, _, _ = layer(x_dev, position_embeddings=pe)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_ms = _timed(dist, e2e_step, args.steps)
+    tokens = B * T * world
+    return {
+        "ms": ms, "tok_s": tokens / (ms * 1e-3), "e2e_tok_s": tokens / (e2e_ms * 1e-3), "e2e_ms": e2e_ms,
+        "h2d": x.numel() * 2, "d2h": out_host.numel() * 2, "stages_ms": st,
+        "roofline": {"bound": "tensor", "kernel": "attn_prefill", "achieved": round(achieved, 1),
+                     "peak": peaks["bf16_sust"], "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_sust"], 4),
+                     "peak_kind": f"{peaks['src']} sustained bf16", "algorithmic_tflop_per_launch": flops / 1e12,
+                     "launch_ms": attn_ms, "traffic": _traffic("attn_prefill")},
+        "layer": layer, "x": x, "pe": pe,
+    }
+
+
+# ------------------------------------------------------------------- decode --
+def bench_decode(args, dist, rank, world, device, peaks):
+    from mka_b200 import StaticKVCache
+    from mka_b200.layers.forward import fastmka_forward
+
+    c = DECODE
+    B, TK, D = c["B"], c["TK"], c["D"]
+    layer = build_layer(c, device, seed=1)
+    cap = TK + 8
+    cache = StaticKVCache(B, c["HKV"], cap, 1, device=device)
+    g = torch.Generator(device=device).manual_seed(2000 + rank)
+    for t in (cache.k[0], cache.v[0]):
+        t.normal_(0.0, 0.1, generator=g)
+    cache._index(layer)
+    x = torch.randn(B, 1, D, generator=g, device=device).to(torch.bfloat16)
+    cos, sin = layer.rotary_emb.cos_sin(torch.tensor([TK], device=device), device)
+    pe = (cos, sin)
+
+    def step():
+        cache.lengths[0] = TK
+        layer(x, position_embeddings=pe, past_key_value=cache)
+
+    for _ in range(args.warmup):
+        step()
+    ms = _timed(dist, step, args.steps)
+    W = layer.prepared(device)
+    kc, vc = cache.k[0], cache.v[0]
+    st = _stage_times(lambda timers: fastmka_forward(x, W, c["H"], c["HKV"], 0.9, False, rope=pe, kv_out=(kc, vc),
+                                                     past_len=TK, timers=timers), max(3, min(args.steps, 10)))
+    attn_ms = st.get("attention", float("nan"))
+    kv_bytes = 2.0 * B * c["HKV"] * (TK + 1) * 128 * 2
+    achieved = kv_bytes / (attn_ms * 1e-3) / 1e9
+    return {
+        "ms": ms, "tok_s": B * world / (ms * 1e-3), "stages_ms": st,
+        "roofline": {"bound": "hbm", "kernel": "attn_decode", "achieved": round(achieved, 1), "peak": peaks["hbm"],
+                     "unit": "GB/s", "frac": round(achieved / peaks["hbm"], 4), "peak_kind": f"{peaks['src']} HBM copy",
+                     "algorithmic_gb_per_launch": kv_bytes / 1e9, "launch_ms": attn_ms,
+                     "traffic": _traffic("attn_decode")},
+    }
+
+
+# -------------------------------------------------------------- CPU (oracle) --
+def _oracle_params(layer):
+    f = lambda t: None if t is None else t.detach().float().cpu()  # noqa: E731
+    return {"wq": f(layer.q_proj.weight), "bq": f(layer.q_proj.bias), "wk": f(layer.k_proj.weight),
+            "bk": f(layer.k_proj.bias), "wv": f(layer.v_proj.weight), "bv": f(layer.v_proj.bias),
+            "wo": f(layer.o_proj.weight), "r1w": f(layer.router[0].weight), "r1b": f(layer.router[0].bias),
+            "r2w": f(layer.router[2].weight), "r2b": f(layer.router[2].bias)}
+
+
+def cpu_reference_step(p, x_cpu, cos, sin):
+    from oracle import fastmka_oracle as orc
+
+    with torch.no_grad():
+        orc.hf_fastmka_forward(x_cpu, p, PREFILL["H"], PREFILL["HKV"], False, 0.9, "silu", cos=cos, sin=sin)
+
+
+def cpu_sample_inputs(seed=0):
+    """One cfg sequence prefix on the CPU: x [1, CPU_SAMPLE_T, D] fp32 and RoPE tables."""
+    c = PREFILL
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(1, CPU_SAMPLE_T, c["D"], generator=g) / math.sqrt(c["D"])
+    rot = _Rotary(c["theta"])
+    cos, sin = rot.cos_sin(torch.arange(CPU_SAMPLE_T), "cpu")
+    return x, cos[:, None], sin[:, None]
+
+
+def cpu_params_random(seed=0):
+    c = PREFILL
+    g = torch.Generator().manual_seed(seed)
+    D, H, HKV, R = c["D"], c["H"], c["HKV"], c["R"]
+    r = lambda *s: torch.randn(*s, generator=g) * 0.02  # noqa: E731
+    return {"wq": r(H * 128, D), "bq": r(H * 128), "wk": r(HKV * 128, D), "bk": r(HKV * 128), "wv": r(HKV * 128, D),
+            "bv": r(HKV * 128), "wo": r(D, H * 128), "r1w": r(R, D), "r1b": r(R), "r2w": r(2, R), "r2b": r(2)}
+
+
+def measure_cpu(p, steps=1):
+    torch.set_num_threads(os.cpu_count() or 1)
+    x, cos, sin = cpu_sample_inputs()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        cpu_reference_step(p, x, cos, sin)
+    dt = (time.perf_counter() - t0) / steps
+    return {"value": CPU_SAMPLE_T / dt, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"reference FastMKA forward (CPU oracle, fp32) on one sequence prefix: batch 1, "
+                      f"seq {CPU_SAMPLE_T} of the prefill config; {dt:.2f} s per step"}
+
+
+def run_reference(args):
+    dist, rank, world, _ = (None, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), 0)
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    p = cpu_params_random()
+    x, cos, sin = cpu_sample_inputs()
+    for _ in range(args.warmup):
+        cpu_reference_step(p, x, cos, sin)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_reference_step(p, x, cos, sin)
+    dt = (time.perf_counter() - t0) / args.steps
+    v = CPU_SAMPLE_T / dt
+    cores = torch.get_num_threads()
+    sample = (f"reference FastMKA forward (CPU oracle restating FastLM/MKA op for op, fp32, {cores} threads) on "
+              f"one sequence prefix per step: batch 1, seq {CPU_SAMPLE_T} of the prefill config")
+    line = {"metric": "FastMKA prefill tokens/s (Qwen-7B-like layer, B200)", "value": v, "unit": "tokens/s",
+            "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "config": _config(args),
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def _config(args):
+    c = PREFILL
+    return {"workload": f"FastMKA attention layer prefill, Qwen-7B-like: batch {c['B']} per GPU, seq {c['T']}, "
+                        f"d_model {c['D']}, {c['H']}/{c['HKV']} heads, head_dim 128, L1+L2, router "
+                        f"{c['D']}->{c['R']}->2, RoPE",
+            "global_batch": c["B"] * args.gpus, "seq_len": c["T"], "parallelism": f"dp{args.gpus} (batch x kv-head units, whole sequences per rank)",
+            "l2": "inputs larger than L2 (X 235 MB per GPU; decode cache 8.6 GB)"}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    dist, rank, world, local = _dist()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    peaks = _peaks()
+    from mka_b200 import ops
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    pre = bench_prefill(args, dist, rank, world, device, peaks)
+    dec = None if args.no_decode else bench_decode(args, dist, rank, world, device, peaks)
+    clocks = sampler.stop()
+    status = ops.device_status()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = measure_cpu(_oracle_params(pre["layer"]))
+    launches_per_step = 5
+    if rank == 0:
+        line = {
+            "metric": "FastMKA prefill tokens/s (Qwen-7B-like layer, B200)",
+            "value": pre["tok_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": pre["ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded N(0,1)/sqrt(d) input, N(0,0.02) weights)",
+            "config": _config(args),
+            "e2e": {"value": pre["e2e_tok_s"], "unit": "tokens/s", "h2d_bytes_per_step": pre["h2d"],
+                    "d2h_bytes_per_step": pre["d2h"], "ms_per_step": pre["e2e_ms"]},
+            "roofline": pre["roofline"],
+            "cpu_baseline": cpu,
+            "gpu_launches": launches_per_step * args.steps,
+            "stages_ms": {k: round(v, 4) for k, v in pre["stages_ms"].items()},
+            "clocks": clocks,
+            "device_status": status,
+        }
+        if dec is not None:
+            d = DECODE
+            line["decode"] = {
+                "metric": "FastMKA decode tokens/s (Llama-3-8B-like layer, batch 64, 32768 cached)",
+                "value": dec["tok_s"], "unit": "tokens/s", "ms_per_step": dec["ms"], "roofline": dec["roofline"],
+                "stages_ms": {k: round(v, 4) for k, v in dec["stages_ms"].items()},
+                "config": {"batch_per_gpu": d["B"], "cache_len": d["TK"], "d_model": d["D"],
+                           "heads": f"{d['H']}/{d['HKV']}"},
+                "gpu_launches": launches_per_step * args.steps,
+            }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -31,7 +31,7 @@ def fastmka_forward(x: torch.Tensor, W: PreparedWeights, num_heads: int, num_kv_
                     past: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
                     rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
                     kv_out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
-                    past_len: Optional[int] = None) -> dict:
+                    past_len: Optional[int] = None, timers: Optional[list] = None) -> dict:
     """Runs the layer on x [B, T, D] (any float dtype; computed in bf16).
 
     past:    (k, v) [B, Hkv, Tp, 128] cached keys/values; the returned k/v are
@@ -40,8 +40,24 @@ def fastmka_forward(x: torch.Tensor, W: PreparedWeights, num_heads: int, num_kv_
              first `past_len` slots are valid; new K/V are written in place at
              [past_len, past_len + T) and the returned k/v are views of the
              valid prefix (no copy of the cache).
+    timers:  if a list is given, (stage, start_event, end_event) CUDA event
+             pairs recorded on the current stream around each launch are appended.
     Returns dict(out [B,T,D] bf16, k, v, lam [B,T,L] fp32, lse).
     """
+    def mark(name):
+        if timers is None:
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        timers.append([name, ev, None])
+        return ev
+
+    def done():
+        if timers is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            timers[-1][2] = ev
+
     if not x.is_cuda:
         raise RuntimeError("the B200 FastMKA forward needs CUDA tensors (there is no CPU fallback)")
     B, T, D = x.shape
@@ -54,8 +70,10 @@ def fastmka_forward(x: torch.Tensor, W: PreparedWeights, num_heads: int, num_kv_
         raise RuntimeError(f"router has {W.levels} outputs but the layer blends {L} levels")
 
     # 1. q (+ RoPE) and router logits
+    mark("qr_proj")
     q, logits = ops.qr_proj(xb.view(B * T, D), W.w_qr, W.b_qr, B, T, num_heads, W.router_hidden, W.w2, L,
                             W.act, rope=rope)
+    done()
     # 2. gate + EMA + blend
     l3 = None
     if use_l3:
@@ -65,7 +83,10 @@ def fastmka_forward(x: torch.Tensor, W: PreparedWeights, num_heads: int, num_kv_
             l3 = l3_memory if l3_memory.dtype == torch.bfloat16 else l3_memory.to(torch.bfloat16)
             if l3.shape[0] != B or l3.shape[2] != D:
                 raise RuntimeError("l3_memory must be [B, T3, D]")
+    mark("route_ema_blend")
     h, lam = ops.route_ema_blend(xb, beta, logits=logits, b2=W.b2, levels=L, l3=l3)
+    done()
+    mark("kv_proj")
     # 3. K/V of the fused memory
     if kv_out is not None:
         kc, vc = kv_out
@@ -86,12 +107,17 @@ def fastmka_forward(x: torch.Tensor, W: PreparedWeights, num_heads: int, num_kv_
                     t_offset=tp)
     else:
         k_tot, v_tot = ops.kv_proj(h.view(B * T, D), W.w_kv, W.b_kv, B, T, num_kv_heads, rope=rope)
+    done()
     # 4. attention
+    mark("attention")
     if T == 1 and k_tot.shape[2] > 1:
         o, lse = ops.attn_decode(q, k_tot, v_tot)
         lse = lse.unsqueeze(-1)
     else:
         o, lse = ops.attn_prefill(q, k_tot, v_tot, causal=True)
+    done()
     # 5. output projection
+    mark("o_proj")
     out = ops.gemm(o.view(B * T, num_heads * HEAD_DIM), W.w_o, W.b_o).view(B, T, D)
+    done()
     return {"out": out, "k": k_tot, "v": v_tot, "lam": lam, "lse": lse, "q": q}
