@@ -137,6 +137,15 @@ using namespace fmka;
 
 namespace {
 inline cudaStream_t as_stream(fmka_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+// The projection epilogues read bias, RoPE rows and router rows as float4.
+int check_epilogue_inputs(const float* bias, const float* cs, const float* sn, int64_t rope_sb, int64_t rope_st,
+                          const char* who) {
+  if (bias != nullptr && !al16(bias)) return set_error(kErrInvalidArgument, std::string(who) + ": bias must be 16-byte aligned");
+  if (cs != nullptr && (!al16(cs) || !al16(sn) || (rope_sb % 4) || (rope_st % 4)))
+    return set_error(kErrInvalidArgument, std::string(who) + ": RoPE tables must be 16-byte aligned with strides % 4 == 0");
+  return kOk;
+}
 inline const __nv_bfloat16* bf(const void* p) { return static_cast<const __nv_bfloat16*>(p); }
 inline __nv_bfloat16* bfw(void* p) { return static_cast<__nv_bfloat16*>(p); }
 
@@ -178,6 +187,7 @@ int fmka_num_sms(void) { return num_sms_current_device(); }
 int fmka_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, const float* bias, void* c, int64_t ldc,
                    int M, int N, int K, fmka_stream_t stream) {
   if (a == nullptr || w == nullptr || c == nullptr) return set_error(kErrInvalidArgument, "gemm: null pointer");
+  if (bias != nullptr && !al16(bias)) return set_error(kErrInvalidArgument, "gemm: bias must be 16-byte aligned");
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
   p.M = M;
@@ -206,6 +216,8 @@ int fmka_qr_proj(const void* x, int64_t ldx, const void* w_qr, int64_t ldw, cons
     return set_error(kErrInvalidArgument, "qr_proj: pass both rope cos and sin or neither");
   if (act != 0 && act != 1) return set_error(kErrInvalidArgument, "qr_proj: act must be 0 (SiLU) or 1 (GELU)");
   if ((q_sb % 8) || (q_sh % 8) || (q_st % 8)) return set_error(kErrInvalidArgument, "qr_proj: q strides % 8");
+  if (int rc = check_epilogue_inputs(bias_qr, rope_cos, rope_sin, rope_sb, rope_st, "qr_proj")) return rc;
+  if (w2 != nullptr && !al16(w2)) return set_error(kErrInvalidArgument, "qr_proj: w2 must be 16-byte aligned");
   const int Nq = Hq * 128;
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
@@ -256,6 +268,7 @@ int fmka_kv_proj(const void* h, int64_t ldh, const void* w_kv, int64_t ldw, cons
   if ((rope_cos == nullptr) != (rope_sin == nullptr))
     return set_error(kErrInvalidArgument, "kv_proj: pass both rope cos and sin or neither");
   if ((kv_sb % 8) || (kv_sh % 8) || (kv_st % 8)) return set_error(kErrInvalidArgument, "kv_proj: kv strides % 8");
+  if (int rc = check_epilogue_inputs(bias_kv, rope_cos, rope_sin, rope_sb, rope_st, "kv_proj")) return rc;
   const int Nk = Hkv * 128;
   GemmParams p;
   std::memset(&p, 0, sizeof(p));

@@ -45,22 +45,24 @@ __device__ __forceinline__ float act_fn(float v, int act) {
   return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));  // GELU (erf form)
 }
 
-// Stores 32 fp32 values (already final) as bf16 to dst (16-byte aligned when
-// all 32 are in range); `nvalid` limits the columns written.
-__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float* v, int nvalid) {
+// Stores 32 fp32 values (held as bits in r) as bf16 to dst; `nvalid` limits
+// the columns written (16-byte vector stores when all 32 fit and dst is aligned).
+__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const uint32_t (&r)[32], int nvalid) {
   if (nvalid >= 32 && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
     uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       uint4 w;
-      w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
-      w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
-      w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
-      w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+      w.x = pack_bf16x2(__uint_as_float(r[q * 8 + 0]), __uint_as_float(r[q * 8 + 1]));
+      w.y = pack_bf16x2(__uint_as_float(r[q * 8 + 2]), __uint_as_float(r[q * 8 + 3]));
+      w.z = pack_bf16x2(__uint_as_float(r[q * 8 + 4]), __uint_as_float(r[q * 8 + 5]));
+      w.w = pack_bf16x2(__uint_as_float(r[q * 8 + 6]), __uint_as_float(r[q * 8 + 7]));
       d4[q] = w;
     }
   } else {
-    for (int j = 0; j < nvalid && j < 32; ++j) dst[j] = __float2bfloat16_rn(v[j]);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < nvalid) dst[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
   }
 }
 
@@ -227,87 +229,152 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(acc_addr + c * 32, r);
           tmem_wait_ld();
           const int n = n0 + c * 32;
-          float v[32];
+          if (sg.bias != nullptr) {
+            if (n + 32 <= sg.n_end) {
+              const float4* b4 = reinterpret_cast<const float4*>(sg.bias + (n - sg.n_begin));
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float b = 0.f;
-            if (sg.bias != nullptr && n + j < sg.n_end) b = __ldg(sg.bias + (n + j - sg.n_begin));
-            v[j] = __uint_as_float(r[j]) + b;
+              for (int q = 0; q < 8; ++q) {
+                const float4 bb = __ldg(b4 + q);
+                r[4 * q + 0] = __float_as_uint(__uint_as_float(r[4 * q + 0]) + bb.x);
+                r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + bb.y);
+                r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + bb.z);
+                r[4 * q + 3] = __float_as_uint(__uint_as_float(r[4 * q + 3]) + bb.w);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n + j < sg.n_end) r[j] = __float_as_uint(__uint_as_float(r[j]) + __ldg(sg.bias + (n + j - sg.n_begin)));
+            }
           }
           if (row_ok && n < sg.n_end) {
-            store_row32(sg.out + (int64_t)m * sg.ld + (n - sg.n_begin), v, sg.n_end - n);
+            store_row32(sg.out + (int64_t)m * sg.ld + (n - sg.n_begin), r, sg.n_end - n);
           }
         }
       } else if (sg.kind == kSegHeads) {
         const int b = row_ok ? m / sg.T : 0;
         const int t = row_ok ? m % sg.T : 0;
-        const int hd = sg.head_dim;  // 128
         const bool rope = sg.rope_cos != nullptr;
-        const float* cs = rope ? sg.rope_cos + (int64_t)b * sg.rope_sb + (int64_t)t * sg.rope_st : nullptr;
-        const float* sn = rope ? sg.rope_sin + (int64_t)b * sg.rope_sb + (int64_t)t * sg.rope_st : nullptr;
+        const int64_t rope_off = (int64_t)b * sg.rope_sb + (int64_t)t * sg.rope_st;
+        __nv_bfloat16* dst_row = sg.out + (int64_t)b * sg.s_b + (int64_t)(t + sg.t_offset) * sg.s_t;
+        // 16-column chunks of the first half of every head (dims d) paired with
+        // the same chunk of the second half (dims d + 64); the RoPE table slice
+        // is loaded once per chunk and shared by the tile's heads.
 #pragma unroll 1
-        for (int hh = 0; hh < BN / 128; ++hh) {
-          const int nl_head = n0 - sg.n_begin + hh * 128;  // first column of this head in the segment
-          const int head = nl_head / hd;
-#pragma unroll 1
-          for (int c2 = 0; c2 < 2; ++c2) {
-            uint32_t r1[32], r2[32];
-            tmem_ld32(acc_addr + hh * 128 + c2 * 32, r1);
-            tmem_ld32(acc_addr + hh * 128 + 64 + c2 * 32, r2);
-            tmem_wait_ld();
-            const bool in_range = (n0 + hh * 128) < sg.n_end;
-            float o1[32], o2[32];
+        for (int c = 0; c < 4; ++c) {
+          float cs1[16], sn1[16], cs2[16], sn2[16];
+          if (rope && row_ok) {
+            const float4* c4a = reinterpret_cast<const float4*>(sg.rope_cos + rope_off + c * 16);
+            const float4* s4a = reinterpret_cast<const float4*>(sg.rope_sin + rope_off + c * 16);
+            const float4* c4b = reinterpret_cast<const float4*>(sg.rope_cos + rope_off + 64 + c * 16);
+            const float4* s4b = reinterpret_cast<const float4*>(sg.rope_sin + rope_off + 64 + c * 16);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int d1 = c2 * 32 + j;
-              const int d2 = d1 + 64;
-              float x1 = __uint_as_float(r1[j]);
-              float x2 = __uint_as_float(r2[j]);
-              if (sg.bias != nullptr && in_range) {
-                x1 += __ldg(sg.bias + nl_head + d1);
-                x2 += __ldg(sg.bias + nl_head + d2);
-              }
-              if (rope && row_ok) {
-                o1[j] = x1 * __ldg(cs + d1) - x2 * __ldg(sn + d1);
-                o2[j] = x2 * __ldg(cs + d2) + x1 * __ldg(sn + d2);
-              } else {
-                o1[j] = x1;
-                o2[j] = x2;
+            for (int q = 0; q < 4; ++q) {
+              const float4 a0 = __ldg(c4a + q), a1 = __ldg(s4a + q), a2 = __ldg(c4b + q), a3 = __ldg(s4b + q);
+              cs1[4 * q] = a0.x; cs1[4 * q + 1] = a0.y; cs1[4 * q + 2] = a0.z; cs1[4 * q + 3] = a0.w;
+              sn1[4 * q] = a1.x; sn1[4 * q + 1] = a1.y; sn1[4 * q + 2] = a1.z; sn1[4 * q + 3] = a1.w;
+              cs2[4 * q] = a2.x; cs2[4 * q + 1] = a2.y; cs2[4 * q + 2] = a2.z; cs2[4 * q + 3] = a2.w;
+              sn2[4 * q] = a3.x; sn2[4 * q + 1] = a3.y; sn2[4 * q + 2] = a3.z; sn2[4 * q + 3] = a3.w;
+            }
+          }
+#pragma unroll
+          for (int hh = 0; hh < BN / 128; ++hh) {
+            uint32_t r1[16], r2[16];
+            tmem_ld16(acc_addr + hh * 128 + c * 16, r1);
+            tmem_ld16(acc_addr + hh * 128 + 64 + c * 16, r2);
+            tmem_wait_ld();
+            const int nl_head = n0 - sg.n_begin + hh * 128;
+            const bool in_range = (n0 + hh * 128) < sg.n_end;
+            if (sg.bias != nullptr && in_range) {
+              const float4* ba = reinterpret_cast<const float4*>(sg.bias + nl_head + c * 16);
+              const float4* bb = reinterpret_cast<const float4*>(sg.bias + nl_head + 64 + c * 16);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float4 x = __ldg(ba + q), y = __ldg(bb + q);
+                r1[4 * q] = __float_as_uint(__uint_as_float(r1[4 * q]) + x.x);
+                r1[4 * q + 1] = __float_as_uint(__uint_as_float(r1[4 * q + 1]) + x.y);
+                r1[4 * q + 2] = __float_as_uint(__uint_as_float(r1[4 * q + 2]) + x.z);
+                r1[4 * q + 3] = __float_as_uint(__uint_as_float(r1[4 * q + 3]) + x.w);
+                r2[4 * q] = __float_as_uint(__uint_as_float(r2[4 * q]) + y.x);
+                r2[4 * q + 1] = __float_as_uint(__uint_as_float(r2[4 * q + 1]) + y.y);
+                r2[4 * q + 2] = __float_as_uint(__uint_as_float(r2[4 * q + 2]) + y.z);
+                r2[4 * q + 3] = __float_as_uint(__uint_as_float(r2[4 * q + 3]) + y.w);
               }
             }
+            uint32_t o1[8], o2[8];
+#pragma unroll
+            for (int j = 0; j < 16; j += 2) {
+              float a0 = __uint_as_float(r1[j]), a1 = __uint_as_float(r1[j + 1]);
+              float b0 = __uint_as_float(r2[j]), b1 = __uint_as_float(r2[j + 1]);
+              if (rope) {
+                const float ra0 = a0 * cs1[j] - b0 * sn1[j];
+                const float ra1 = a1 * cs1[j + 1] - b1 * sn1[j + 1];
+                const float rb0 = b0 * cs2[j] + a0 * sn2[j];
+                const float rb1 = b1 * cs2[j + 1] + a1 * sn2[j + 1];
+                a0 = ra0; a1 = ra1; b0 = rb0; b1 = rb1;
+              }
+              o1[j / 2] = pack_bf16x2(a0, a1);
+              o2[j / 2] = pack_bf16x2(b0, b1);
+            }
             if (row_ok && in_range) {
-              __nv_bfloat16* dst =
-                  sg.out + (int64_t)b * sg.s_b + (int64_t)head * sg.s_h + (int64_t)(t + sg.t_offset) * sg.s_t;
-              store_row32(dst + c2 * 32, o1, 32);
-              store_row32(dst + 64 + c2 * 32, o2, 32);
+              __nv_bfloat16* dst = dst_row + (int64_t)(nl_head / 128) * sg.s_h;
+              uint4* d1 = reinterpret_cast<uint4*>(dst + c * 16);
+              uint4* d2 = reinterpret_cast<uint4*>(dst + 64 + c * 16);
+              d1[0] = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+              d1[1] = make_uint4(o1[4], o1[5], o1[6], o1[7]);
+              d2[0] = make_uint4(o2[0], o2[1], o2[2], o2[3]);
+              d2[1] = make_uint4(o2[4], o2[5], o2[6], o2[7]);
             }
           }
         }
       } else {  // kSegRouter
         float part[4] = {0.f, 0.f, 0.f, 0.f};
         const int R = sg.n_end - sg.n_begin;
+        const int L = sg.L;
+        const int act = sg.act;
+        const float* w2 = sg.w2;
+        const float* bias = sg.bias;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
+          const int nl = n0 - sg.n_begin + c * 32;
           uint32_t r[32];
           tmem_ld32(acc_addr + c * 32, r);
           tmem_wait_ld();
-          const int nl = n0 - sg.n_begin + c * 32;
-#pragma unroll 4
-          for (int j = 0; j < 32; ++j) {
-            if (nl + j < R) {
-              float v = __uint_as_float(r[j]);
-              if (sg.bias != nullptr) v += __ldg(sg.bias + nl + j);
-              const float a = act_fn(v, sg.act);
+          if (nl >= R) continue;  // warp-uniform
+          if (nl + 32 <= R && (R & 3) == 0) {
 #pragma unroll
-              for (int l = 0; l < 4; ++l)
-                if (l < sg.L) part[l] += __ldg(sg.w2 + (int64_t)l * R + nl + j) * a;
+            for (int q = 0; q < 8; ++q) {
+              float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (bias != nullptr) bb = __ldg(reinterpret_cast<const float4*>(bias + nl) + q);
+              const float a0 = act_fn(__uint_as_float(r[4 * q + 0]) + bb.x, act);
+              const float a1 = act_fn(__uint_as_float(r[4 * q + 1]) + bb.y, act);
+              const float a2 = act_fn(__uint_as_float(r[4 * q + 2]) + bb.z, act);
+              const float a3 = act_fn(__uint_as_float(r[4 * q + 3]) + bb.w, act);
+#pragma unroll
+              for (int l = 0; l < 4; ++l) {
+                if (l < L) {
+                  const float4 w = __ldg(reinterpret_cast<const float4*>(w2 + (int64_t)l * R + nl) + q);
+                  part[l] += w.x * a0 + w.y * a1 + w.z * a2 + w.w * a3;
+                }
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (nl + j < R) {
+                float v = __uint_as_float(r[j]);
+                if (bias != nullptr) v += __ldg(bias + nl + j);
+                const float a = act_fn(v, act);
+#pragma unroll
+                for (int l = 0; l < 4; ++l)
+                  if (l < L) part[l] += __ldg(w2 + (int64_t)l * R + nl + j) * a;
+              }
             }
           }
         }
         if (row_ok) {
 #pragma unroll
           for (int l = 0; l < 4; ++l)
-            if (l < sg.L) atomicAdd(sg.logits + (int64_t)m * sg.L + l, part[l]);
+            if (l < L) atomicAdd(sg.logits + (int64_t)m * L + l, part[l]);
         }
       }
       tc_fence_before();
