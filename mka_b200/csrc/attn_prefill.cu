@@ -9,19 +9,24 @@
 // uses the same Tk - Tq causal offset). GQA is handled by indexing the shared
 // K/V head instead of materialising _repeat_kv (hf/attention.py:28-33,128-129).
 //
-// One CTA per (128-query tile, query head). Warp roles:
-//   warp 0      TMA producer: Q once, then K and V tiles (128 keys) into a
+// One CTA per (256-query block, query head): two 128-row Q tiles share every
+// K/V tile. Warp roles (12 warps, 3 warpgroups):
+//   warp 0      TMA producer: Q0, Q1 once, then K and V tiles (128 keys) into a
 //               two-stage shared-memory ring (128-byte swizzle)
-//   warp 1      MMA issuer: S_j = Q K_j^T into one of two TMEM S buffers; then
-//               O += P_{j-1} V_{j-1} with P read straight from TMEM
-//   warp 2      TMEM allocator (512 columns: S0 | S1 | O)
-//   warps 4..7  softmax: thread i owns query row i; reads its S row from TMEM,
-//               applies the causal mask on diagonal tiles, keeps the running
-//               max m and sum z (online softmax), writes P as packed bf16 back
-//               over S, rescales O in TMEM only when the max grew by more than
-//               2^8 (exact: the final 1/z uses the same stale max), and at the
-//               end normalises O and writes O and LSE.
-// KV tiles past the causal limit of the query tile are never loaded.
+//   warp 1      TMEM allocator (512 columns: S0 | S1 | O0 | O1), then the MMA
+//               issuer: S_i = Q_i K_j^T, and O_i += P_i V_j with P read straight
+//               from TMEM (written there over S_i), interleaved so one tile's
+//               GEMMs run while the other tile's softmax runs
+//   warps 2,3   idle (complete the first warpgroup)
+//   warps 4..7  softmax of Q tile 0, warps 8..11 softmax of Q tile 1: thread =
+//               query row; reads its S row from TMEM, causal mask on diagonal
+//               tiles, running max m and sum z, writes P (bf16) back over S,
+//               rescales O in TMEM only when the max grew by more than 2^8
+//               (exact: the final 1/z uses the same stale max). A quarter of
+//               the exponentials run on the FMA pipe (exp2_poly) so the
+//               special-function unit does not bound the loop. At the end the
+//               warpgroup normalises O and writes O and LSE.
+// KV tiles past a Q tile's causal limit are neither loaded nor multiplied.
 #include "fmka_internal.h"
 #include "ptx.cuh"
 
@@ -29,14 +34,26 @@ namespace fmka {
 
 namespace {
 
-constexpr int kBM = 128;
-constexpr int kBN = 128;
+constexpr int kBM = 128;        // rows per Q tile
+constexpr int kQTiles = 2;      // Q tiles per CTA
+constexpr int kBlockRows = kBM * kQTiles;
+constexpr int kBN = 128;        // keys per K/V tile
 constexpr int kHeadDim = 128;
-constexpr int kKS = 2;
-constexpr int kThreads = 256;
-constexpr int kTileBytes = 128 * 128 * 2;  // 32 KB
+constexpr int kKS = 2;          // K/V ring stages
+constexpr int kThreads = 384;  // 3 warpgroups
+// Register split (setmaxnreg): the producer/MMA warpgroup gives registers to
+// the two softmax warpgroups. The launch holds kThreads x (registers ptxas
+// assigned); the split must fit in it or setmaxnreg.inc would wait forever, so
+// the launcher checks kMinLaunchRegs against the compiled kernel first.
+#ifndef FMKA_ATTN_REG_SPLIT
+#define FMKA_ATTN_REG_SPLIT 0
+#endif
+constexpr int kRegsControl = 40;
+constexpr int kRegsSoftmax = 232;
+constexpr int kMinLaunchRegs = (128 * kRegsControl + 256 * kRegsSoftmax + kThreads - 1) / kThreads;
+constexpr int kTileBytes = 128 * 128 * 2;   // 32 KB
 constexpr int kHalfBytes = kTileBytes / 2;  // one 64-column swizzle box
-constexpr int kSmemBytes = kTileBytes * (1 + 2 * kKS) + 1024 + 256;
+constexpr int kSmemBytes = kTileBytes * (kQTiles + 2 * kKS) + 1024 + 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct AttnParams {
@@ -47,37 +64,63 @@ struct AttnParams {
   int64_t o_sb, o_st, o_sh;
   float* lse;        // lse[b, h, t] (may be null)
   int64_t lse_sb, lse_sh;
-  int n_qtiles;
+  int n_qblocks;
   uint32_t* status;
 };
+
+// 2^x for a pair on the FMA pipe: Cody-Waite split x = n + f with n = round(x),
+// f in [-1/2, 1/2]; 2^f from a degree-3 polynomial fitted here by minimax on the
+// relative error (max 8.4e-5, well below the bf16 rounding of P); 2^n added to
+// the exponent bits. Inputs below -126 return 2^-126.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -126.0f);
+  x.y = fmaxf(x.y, -126.0f);
+  const float2 t = fadd2(x, make_float2(12582912.0f, 12582912.0f));
+  const float2 r = fadd2(t, make_float2(-12582912.0f, -12582912.0f));
+  const float2 f = ffma2(r, make_float2(-1.0f, -1.0f), x);
+  float2 p = ffma2(make_float2(0.055212993174791336f, 0.055212993174791336f), f,
+                   make_float2(0.24271413683891296f, 0.24271413683891296f));
+  p = ffma2(p, f, make_float2(0.6932621598243713f, 0.6932621598243713f));
+  p = ffma2(p, f, make_float2(0.999919593334198f, 0.999919593334198f));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
+__device__ __forceinline__ int kv_tiles_for(int r0, int Tq, int Tk, int offset, int causal) {
+  if (r0 >= Tq) return 0;
+  if (!causal) return (Tk + kBN - 1) / kBN;
+  int last = r0 + kBM - 1 + offset;
+  if (last > Tk - 1) last = Tk - 1;
+  return last < 0 ? 0 : last / kBN + 1;
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
     attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + kTileBytes;
-  uint8_t* sV = sK + kKS * kTileBytes;
+  uint8_t* sQ = smem;                                // [2][32 KB]
+  uint8_t* sK = smem + kQTiles * kTileBytes;         // [kKS][32 KB]
+  uint8_t* sV = sK + kKS * kTileBytes;               // [kKS][32 KB]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kKS * kTileBytes);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = k_full + kKS;
-  uint64_t* v_full = k_empty + kKS;
-  uint64_t* v_empty = v_full + kKS;
-  uint64_t* s_full = v_empty + kKS;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* pv_bar = p_full + 2;   // [2]: PV_i completes pv_bar[i & 1]
-  uint64_t* o_full = pv_bar + 2;   // the last PV has completed
-  uint64_t* mma_done = o_full + 1;
+  uint64_t* q_full = bars;             // [2]
+  uint64_t* k_full = q_full + 2;       // [kKS]
+  uint64_t* k_empty = k_full + kKS;    // [kKS]
+  uint64_t* v_full = k_empty + kKS;    // [kKS]
+  uint64_t* v_empty = v_full + kKS;    // [kKS]
+  uint64_t* s_full = v_empty + kKS;    // [2] per Q tile
+  uint64_t* p_full = s_full + 2;       // [2] per Q tile
+  uint64_t* pv_bar = p_full + 2;       // [2][2]: PV of tile i, kv step j completes pv_bar[2i + (j & 1)]
+  uint64_t* o_full = pv_bar + 4;       // [2] the last PV of tile i has completed
+  uint64_t* mma_done = o_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
   const int lane = lane_id();
 
-  // ---- tile coordinates: the G query heads of one KV head are adjacent, heavy
-  // (late) query tiles first ----
+  // ---- block coordinates: the G query heads of one KV head are adjacent,
+  // heavy (late) query blocks first ----
   const int G = p.Hq / p.Hkv;
   int idx = blockIdx.x;
   const int g = idx % G;
@@ -86,34 +129,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   idx /= p.Hkv;
   const int b = idx % p.B;
   idx /= p.B;
-  const int qt = p.n_qtiles - 1 - idx;
+  const int qb = p.n_qblocks - 1 - idx;
   const int hq = hkv * G + g;
-  const int q0 = qt * kBM;
+  const int q0 = qb * kBlockRows;
   const int offset = p.Tk - p.Tq;
-  int n_kv;
-  if (p.causal) {
-    int last = q0 + kBM - 1 + offset;
-    if (last > p.Tk - 1) last = p.Tk - 1;
-    n_kv = last < 0 ? 0 : last / kBN + 1;
-  } else {
-    n_kv = (p.Tk + kBN - 1) / kBN;
-  }
+  const int n0 = kv_tiles_for(q0, p.Tq, p.Tk, offset, p.causal);
+  const int n1 = kv_tiles_for(q0 + kBM, p.Tq, p.Tk, offset, p.causal);
+  const int n_load = n0 > n1 ? n0 : n1;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+    }
     for (int s = 0; s < kKS; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], 128);
-    }
-    mbar_init(&pv_bar[0], 1);
-    mbar_init(&pv_bar[1], 1);
-    mbar_init(o_full, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&pv_bar[i], 1);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -123,7 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
   }
-  if (warp == 2) {
+  if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -131,16 +168,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  constexpr uint32_t kColO = 256;
+
+#if FMKA_ATTN_REG_SPLIT
+  if (warp < 4) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
+  else asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
+#endif
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, kTileBytes);
-      tma_load_4d(sQ, &tmQ, q_full, 0, q0, hq, b);
-      tma_load_4d(sQ + kHalfBytes, &tmQ, q_full, 64, q0, hq, b);
+      const int nt[2] = {n0, n1};
+      for (int i = 0; i < kQTiles; ++i) {
+        if (nt[i] == 0) continue;
+        mbar_arrive_expect_tx(&q_full[i], kTileBytes);
+        tma_load_4d(sQ + i * kTileBytes, &tmQ, &q_full[i], 0, q0 + i * kBM, hq, b);
+        tma_load_4d(sQ + i * kTileBytes + kHalfBytes, &tmQ, &q_full[i], 64, q0 + i * kBM, hq, b);
+      }
       int last_k = -1, last_v = -1;
-      for (int j = 0; j < n_kv && !*abort_flag; ++j) {
+      for (int j = 0; j < n_load && !*abort_flag; ++j) {
         const int ks = j % kKS;
         const uint32_t ph = (j / kKS) & 1;
         if (!mbar_wait(&k_empty[ks], ph ^ 1u, p.status)) {
@@ -162,7 +207,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Drain: every issued TMA load has landed before teardown (on the normal
       // path the MMA warp has already consumed them all).
-      mbar_wait(q_full, 0, p.status);
+      for (int i = 0; i < kQTiles; ++i)
+        if (nt[i] > 0) mbar_wait(&q_full[i], 0, p.status);
       for (int j = last_k; j >= 0 && j > last_k - kKS; --j) mbar_wait(&k_full[j % kKS], (j / kKS) & 1, p.status);
       for (int j = last_v; j >= 0 && j > last_v - kKS; --j) mbar_wait(&v_full[j % kKS], (j / kKS) & 1, p.status);
     }
@@ -171,97 +217,124 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t id_s = make_idesc_bf16(kBM, kBN, false, false);
       constexpr uint32_t id_pv = make_idesc_bf16(kBM, kHeadDim, false, true);
-      const uint32_t q_addr = smem_u32(sQ);
-      auto issue_pv = [&](int i) -> bool {
-        const int vs = i % kKS;
-        const uint32_t vph = (i / kKS) & 1;
-        if (!mbar_wait(&v_full[vs], vph, p.status)) return false;
-        if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1, p.status)) return false;
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(sV + vs * kTileBytes);
-        const uint32_t p_tmem = tmem + (i & 1) * 128;
-#pragma unroll
-        for (int k = 0; k < kBN / 16; ++k) {
-          umma_ts(tmem + kColO, p_tmem + k * 8, desc_mnmajor_sw128(v_addr + k * 2048, kHalfBytes), id_pv,
-                  (i > 0 || k > 0) ? 1u : 0u);
-        }
-        tc_commit(&pv_bar[i & 1]);
-        tc_commit(&v_empty[vs]);
-        if (i == n_kv - 1) tc_commit(o_full);
-        return true;
-      };
-      bool ok = mbar_wait(q_full, 0, p.status);
-      if (ok) tc_fence_after();
-      for (int j = 0; ok && j < n_kv; ++j) {
+      const int nt[2] = {n0, n1};
+      bool ok = true;
+      auto issue_s = [&](int i, int j) {
+        if (!ok) return;
         const int ks = j % kKS;
-        const uint32_t kph = (j / kKS) & 1;
-        if (!mbar_wait(&k_full[ks], kph, p.status)) {
+        if (!mbar_wait(&k_full[ks], (j / kKS) & 1, p.status)) {
           ok = false;
-          break;
+          return;
         }
         tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQ + i * kTileBytes);
         const uint32_t k_addr = smem_u32(sK + ks * kTileBytes);
-        const uint32_t d = tmem + (j & 1) * 128;
+        const uint32_t d = tmem + i * 128;
 #pragma unroll
         for (int k = 0; k < kHeadDim / 16; ++k) {
           const uint32_t off = (k >> 2) * kHalfBytes + (k & 3) * 32;
           umma_ss(d, desc_kmajor_sw128(q_addr + off), desc_kmajor_sw128(k_addr + off), id_s, k > 0 ? 1u : 0u);
         }
-        tc_commit(&s_full[j & 1]);
-        tc_commit(&k_empty[ks]);
-        if (j >= 1 && !issue_pv(j - 1)) {
+        tc_commit(&s_full[i]);
+      };
+      auto issue_pv = [&](int i, int j) {
+        if (!ok) return;
+        const int vs = j % kKS;
+        if (!mbar_wait(&v_full[vs], (j / kKS) & 1, p.status) || !mbar_wait(&p_full[i], j & 1, p.status)) {
           ok = false;
-          break;
+          return;
         }
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sV + vs * kTileBytes);
+        const uint32_t p_tmem = tmem + i * 128;
+        const uint32_t o_tmem = tmem + 256 + i * 128;
+#pragma unroll
+        for (int k = 0; k < kBN / 16; ++k) {
+          umma_ts(o_tmem, p_tmem + k * 8, desc_mnmajor_sw128(v_addr + k * 2048, kHalfBytes), id_pv,
+                  (j > 0 || k > 0) ? 1u : 0u);
+        }
+        tc_commit(&pv_bar[2 * i + (j & 1)]);
+        if (j == nt[i] - 1) tc_commit(&o_full[i]);
+      };
+      for (int i = 0; i < kQTiles; ++i)
+        if (nt[i] > 0 && !mbar_wait(&q_full[i], 0, p.status)) ok = false;
+      if (ok) tc_fence_after();
+      for (int i = 0; i < kQTiles; ++i)
+        if (nt[i] > 0) issue_s(i, 0);
+      if (ok && n_load > 0) tc_commit(&k_empty[0]);
+      for (int j = 0; ok && j < n_load; ++j) {
+        for (int i = 0; i < kQTiles; ++i) {
+          if (j < nt[i]) issue_pv(i, j);
+          if (j + 1 < nt[i]) issue_s(i, j + 1);
+        }
+        if (!ok) break;
+        tc_commit(&v_empty[j % kKS]);
+        if (j + 1 < n_load) tc_commit(&k_empty[(j + 1) % kKS]);
         if (*abort_flag) ok = false;
       }
-      if (ok && n_kv > 0) ok = issue_pv(n_kv - 1);
       if (!ok) *abort_flag = 1;
       tc_commit(mma_done);
       mbar_wait(mma_done, 0, p.status);
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------- softmax --
-    const int r = (warp - 4) * 32 + lane;
-    const int q = q0 + r;
+    const int ti = (warp - 4) / 4;  // Q tile of this warpgroup
+    const int quarter = warp & 3;   // TMEM lane quarter this warp may access
+    const int r = quarter * 32 + lane;
+    const int q = q0 + ti * kBM + r;
+    const int n_kv = ti == 0 ? n0 : n1;
     const int qlim = p.causal ? q + offset : p.Tk - 1;  // last visible key
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp - 4) * 32) << 16);
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t s_col = ti * 128;
+    const uint32_t o_col = 256 + ti * 128;
     float m_used = -INFINITY;
     float z = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      const int buf = j & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[buf], (j >> 1) & 1, p.status))) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[ti], j & 1, p.status))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t s[128];
-      tmem_ld32(lane_addr + buf * 128 + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-      tmem_ld32(lane_addr + buf * 128 + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
-      tmem_ld32(lane_addr + buf * 128 + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
-      tmem_ld32(lane_addr + buf * 128 + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
-      tmem_wait_ld();
       const int kbase = j * kBN;
-      if (kbase + kBN - 1 > qlim) {
+      const bool diag = kbase + kBN - 1 > qlim;  // this tile needs the causal / length mask
+      // ---- pass 1: row max over the 128 scores ----
+      float mx0;
+      {
+        uint32_t s[128];
+        tmem_ld32(lane_addr + s_col + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+        tmem_ld32(lane_addr + s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+        tmem_ld32(lane_addr + s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
+        tmem_ld32(lane_addr + s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
+        tmem_wait_ld();
+        if (diag) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (kbase + c > qlim) s[c] = 0xFF800000u;  // -inf
+          for (int c = 0; c < 128; ++c)
+            if (kbase + c > qlim) s[c] = 0xFF800000u;  // -inf
+        }
+        // eight independent chains of three-input maxima
+        float mxa[8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) mxa[a] = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 128; c += 16) {
+#pragma unroll
+          for (int a = 0; a < 8; ++a) mxa[a] = fmax3(mxa[a], __uint_as_float(s[c + a]), __uint_as_float(s[c + 8 + a]));
+        }
+        mx0 = fmax3(fmax3(mxa[0], mxa[1], mxa[2]), fmax3(mxa[3], mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7]));
       }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
-      mx *= p.scale_log2;
+      const float mx = mx0 * p.scale_log2;
       float alpha = 1.f;
-      // The decision is warp-uniform (tcgen05.ld/st are warp-collective): when
-      // any row of the warp needs a larger max, every row of the warp moves its
-      // max up to max(m_used, mx), which is always valid for the online softmax.
+      // Warp-uniform decision (tcgen05.ld/st are warp-collective): when any row
+      // needs a larger max, every row of the warp moves its max up to
+      // max(m_used, mx), which is always valid for the online softmax.
       if (__any_sync(0xffffffffu, mx > m_used + kRescaleThreshold)) {
         const float m_new = fmaxf(m_used, mx);
         alpha = (m_new == m_used) ? 1.f : fast_exp2(m_used - m_new);  // 0 on the first tile
         if (j > 0) {
           // O holds P_0..P_{j-1} V: wait for the last PV, then rescale it.
-          if (!__all_sync(0xffffffffu, mbar_wait(&pv_bar[(j - 1) & 1], ((j - 1) >> 1) & 1, p.status))) {
+          if (!__all_sync(0xffffffffu,
+                          mbar_wait(&pv_bar[2 * ti + ((j - 1) & 1)], ((j - 1) >> 1) & 1, p.status))) {
             ok = false;
             break;
           }
@@ -269,70 +342,94 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
           for (int c4 = 0; c4 < 4; ++c4) {
             uint32_t o[32];
-            tmem_ld32(lane_addr + kColO + c4 * 32, o);
+            tmem_ld32(lane_addr + o_col + c4 * 32, o);
             tmem_wait_ld();
 #pragma unroll
             for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-            tmem_st32(lane_addr + kColO + c4 * 32, o);
+            tmem_st32(lane_addr + o_col + c4 * 32, o);
           }
         }
         m_used = m_new;
       }
+      // ---- pass 2: P = 2^(s * scale - m) chunk by chunk; P chunk c (16 packed
+      // columns) lands on columns already consumed ----
       const float msub = (m_used == -INFINITY) ? 0.f : m_used;
-      float rowsum = 0.f;
-      uint32_t pk[64];
+      const float2 sl2 = make_float2(p.scale_log2, p.scale_log2);
+      const float2 nm2 = make_float2(-msub, -msub);
+      float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = fast_exp2(__uint_as_float(s[2 * c]) * p.scale_log2 - msub);
-        const float p1 = fast_exp2(__uint_as_float(s[2 * c + 1]) * p.scale_log2 - msub);
-        rowsum += p0 + p1;
-        pk[c] = pack_bf16x2(p0, p1);
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t s[32];
+        tmem_ld32(lane_addr + s_col + 32 * ch, s);
+        tmem_wait_ld();
+        if (diag) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (kbase + 32 * ch + c > qlim) s[c] = 0xFF800000u;
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const float2 xx = ffma2(make_float2(__uint_as_float(s[2 * c]), __uint_as_float(s[2 * c + 1])), sl2, nm2);
+          float2 pp;
+          if ((c & 3) == 3) {
+            pp = exp2_poly2(xx);
+          } else {
+            pp.x = fast_exp2(xx.x);
+            pp.y = fast_exp2(xx.y);
+          }
+          acc[c & 3] = fadd2(acc[c & 3], pp);
+          pk[c] = pack_bf16x2(pp.x, pp.y);
+        }
+        tmem_st16(lane_addr + s_col + 16 * ch, pk);
       }
-      z = z * alpha + rowsum;
-      tmem_st32(lane_addr + buf * 128 + 0, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-      tmem_st32(lane_addr + buf * 128 + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+      const float2 a01 = fadd2(acc[0], acc[1]);
+      const float2 a23 = fadd2(acc[2], acc[3]);
+      const float2 asum = fadd2(a01, a23);
+      z = z * alpha + (asum.x + asum.y);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[buf]);
+      mbar_arrive(&p_full[ti]);
     }
     if (!ok) *abort_flag = 1;
     // ---- epilogue: O / z and LSE ----
-    if (__all_sync(0xffffffffu, ok && n_kv > 0 && mbar_wait(o_full, 0, p.status))) {
-      tc_fence_after();
-      const float inv = z > 0.f ? 1.f / z : 0.f;
-      const bool row_ok = q < p.Tq;
-      __nv_bfloat16* dst = p.o + (int64_t)b * p.o_sb + (int64_t)q * p.o_st + (int64_t)hq * p.o_sh;
+    if (n_kv > 0) {
+      if (__all_sync(0xffffffffu, ok && mbar_wait(&o_full[ti], 0, p.status))) {
+        tc_fence_after();
+        const float inv = z > 0.f ? 1.f / z : 0.f;
+        const bool row_ok = q < p.Tq;
+        __nv_bfloat16* dst = p.o + (int64_t)b * p.o_sb + (int64_t)q * p.o_st + (int64_t)hq * p.o_sh;
 #pragma unroll 1
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t o[32];
-        tmem_ld32(lane_addr + kColO + c4 * 32, o);
-        tmem_wait_ld();
-        if (row_ok) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t o[32];
+          tmem_ld32(lane_addr + o_col + c4 * 32, o);
+          tmem_wait_ld();
+          if (row_ok) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(o[v * 8 + 0]) * inv, __uint_as_float(o[v * 8 + 1]) * inv);
-            w.y = pack_bf16x2(__uint_as_float(o[v * 8 + 2]) * inv, __uint_as_float(o[v * 8 + 3]) * inv);
-            w.z = pack_bf16x2(__uint_as_float(o[v * 8 + 4]) * inv, __uint_as_float(o[v * 8 + 5]) * inv);
-            w.w = pack_bf16x2(__uint_as_float(o[v * 8 + 6]) * inv, __uint_as_float(o[v * 8 + 7]) * inv);
-            d4[v] = w;
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(o[v * 8 + 0]) * inv, __uint_as_float(o[v * 8 + 1]) * inv);
+              w.y = pack_bf16x2(__uint_as_float(o[v * 8 + 2]) * inv, __uint_as_float(o[v * 8 + 3]) * inv);
+              w.z = pack_bf16x2(__uint_as_float(o[v * 8 + 4]) * inv, __uint_as_float(o[v * 8 + 5]) * inv);
+              w.w = pack_bf16x2(__uint_as_float(o[v * 8 + 6]) * inv, __uint_as_float(o[v * 8 + 7]) * inv);
+              d4[v] = w;
+            }
           }
         }
+        if (row_ok && p.lse != nullptr) {
+          p.lse[(int64_t)b * p.lse_sb + (int64_t)hq * p.lse_sh + q] = m_used * 0.69314718055994531f + __logf(z);
+        }
+      } else {
+        *abort_flag = 1;
       }
-      if (row_ok && p.lse != nullptr) {
-        p.lse[(int64_t)b * p.lse_sb + (int64_t)hq * p.lse_sh + q] =
-            m_used * 0.69314718055994531f + __logf(z);
-      }
-    } else if (n_kv > 0) {
-      *abort_flag = 1;
     }
   }
 
   __syncwarp();
   tc_fence_before();
   __syncthreads();
-  if (warp == 2) {
+  if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -388,14 +485,23 @@ int launch_attn_prefill(const __nv_bfloat16* q, int64_t q_sb, int64_t q_sh, int6
   p.lse = lse;
   p.lse_sb = lse_sb;
   p.lse_sh = lse_sh;
-  p.n_qtiles = (Tq + kBM - 1) / kBM;
+  p.n_qblocks = (Tq + kBlockRows - 1) / kBlockRows;
   p.status = device_status_word();
-  const int64_t grid = (int64_t)p.n_qtiles * B * Hq;
+  const int64_t grid = (int64_t)p.n_qblocks * B * Hq;
   if (grid > 0x7FFFFFFF) return set_error(kErrUnsupported, "attn_prefill: problem too large");
   int rc = check_cuda(cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            kSmemBytes),
                       "attn_prefill attr");
   if (rc) return rc;
+  static int launch_regs = 0;
+  if (launch_regs == 0) {
+    cudaFuncAttributes fa;
+    rc = check_cuda(cudaFuncGetAttributes(&fa, attn_prefill_kernel), "attn_prefill attributes");
+    if (rc) return rc;
+    launch_regs = fa.numRegs;
+  }
+  if (FMKA_ATTN_REG_SPLIT && launch_regs < kMinLaunchRegs)
+    return set_error(kErrUnsupported, "attn_prefill: compiled register count too small for the warpgroup register split");
   attn_prefill_kernel<<<(unsigned)grid, kThreads, kSmemBytes, stream>>>(tmQ, tmK, tmV, p);
   return check_cuda(cudaGetLastError(), "attn_prefill launch");
 }
