@@ -61,7 +61,8 @@ def build(force: bool = False, verbose: bool = False, jobs: int = 0) -> Path:
     for src in SOURCES:
         obj = obj_dir / (Path(src).stem + ".o")
         objs.append(obj)
-        cmd = [nvcc, *NVCC_FLAGS, "-I", str(INCLUDE), "-c", str(CSRC / src), "-o", str(obj)]
+        extra = os.environ.get("FMKA_NVCC_DEFINES", "").split()
+        cmd = [nvcc, *NVCC_FLAGS, *extra, "-I", str(INCLUDE), "-c", str(CSRC / src), "-o", str(obj)]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
             print(" ".join(cmd), flush=True)

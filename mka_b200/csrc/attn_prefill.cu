@@ -22,9 +22,9 @@
 //               query row; reads its S row from TMEM, causal mask on diagonal
 //               tiles, running max m and sum z, writes P (bf16) back over S,
 //               rescales O in TMEM only when the max grew by more than 2^8
-//               (exact: the final 1/z uses the same stale max). A quarter of
-//               the exponentials run on the FMA pipe (exp2_poly) so the
-//               special-function unit does not bound the loop. At the end the
+//               (exact: the final 1/z uses the same stale max). One pair
+//               of exponentials in eight runs on the FMA pipe (exp2_poly2)
+//               to relieve the special-function unit. At the end the
 //               warpgroup normalises O and writes O and LSE.
 // KV tiles past a Q tile's causal limit are neither loaded nor multiplied.
 #include "fmka_internal.h"
@@ -55,6 +55,22 @@ constexpr int kTileBytes = 128 * 128 * 2;   // 32 KB
 constexpr int kHalfBytes = kTileBytes / 2;  // one 64-column swizzle box
 constexpr int kSmemBytes = kTileBytes * (kQTiles + 2 * kKS) + 1024 + 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// One pair in every kPolyEvery pairs of exponentials runs on the FMA pipe.
+#ifndef FMKA_POLY_EVERY
+#define FMKA_POLY_EVERY 8
+#endif
+// Pack P to bf16 with integer rounding (ALU pipe) instead of cvt (XU pipe).
+#ifndef FMKA_PACK_ALU
+#define FMKA_PACK_ALU 0
+#endif
+
+// bf16x2 of two non-negative finite floats, rounded to nearest (ties away
+// from zero) on the integer ALU: add half an ulp of bf16, keep the high halves.
+__device__ __forceinline__ uint32_t pack_bf16x2_alu(float lo, float hi) {
+  const uint32_t a = __float_as_uint(lo) + 0x8000u;
+  const uint32_t b = __float_as_uint(hi) + 0x8000u;
+  return __byte_perm(a, b, 0x7632);
+}
 
 struct AttnParams {
   int B, Hq, Hkv, Tq, Tk;
@@ -372,14 +388,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 16; ++c) {
           const float2 xx = ffma2(make_float2(__uint_as_float(s[2 * c]), __uint_as_float(s[2 * c + 1])), sl2, nm2);
           float2 pp;
-          if ((c & 3) == 3) {
+          if ((c % FMKA_POLY_EVERY) == FMKA_POLY_EVERY - 1) {
             pp = exp2_poly2(xx);
           } else {
             pp.x = fast_exp2(xx.x);
             pp.y = fast_exp2(xx.y);
           }
           acc[c & 3] = fadd2(acc[c & 3], pp);
+#if FMKA_PACK_ALU
+          pk[c] = pack_bf16x2_alu(pp.x, pp.y);
+#else
           pk[c] = pack_bf16x2(pp.x, pp.y);
+#endif
         }
         tmem_st16(lane_addr + s_col + 16 * ch, pk);
       }
