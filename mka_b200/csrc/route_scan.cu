@@ -21,7 +21,9 @@
 // aggregate, then walks back over published aggregates until it finds a
 // published inclusive state. Chunk order comes from an atomic ticket, so a CTA
 // only ever waits on CTAs that started before it. Waits are bounded; a timeout
-// sets a status bit and the scan continues with a zero contribution.
+// sets a status bit and the scan continues with a zero contribution. Four CTAs
+// share an SM (64 registers a thread) so that one CTA's look-back latency is
+// covered by the others' loads.
 #include "fmka_internal.h"
 #include "ptx.cuh"
 
@@ -35,6 +37,9 @@ constexpr int kWarps = 8;
 constexpr int kTokPerWarp = kChunkT / kWarps;  // 8
 constexpr int kThreads = kWarps * 32;
 
+#ifndef FMKA_SCAN_MINB
+#define FMKA_SCAN_MINB 4
+#endif
 constexpr uint32_t kFlagAgg = 1;
 constexpr uint32_t kFlagInc = 2;
 
@@ -83,7 +88,90 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
   f[7] = bf16hi_to_f32(u.w);
 }
 
-__global__ void __launch_bounds__(kThreads, 2) route_ema_blend_kernel(const __grid_constant__ ScanParams p) {
+// Warp 0 of the CTA that owns (seq, chunk): publishes the chunk aggregate `a`
+// (state after the chunk from a zero state, this lane's 8 channels), finds the
+// state entering the chunk by the decoupled look-back, publishes the chunk's
+// inclusive state and returns the incoming state in sin_.
+__device__ __forceinline__ void chunk_lookback(const ScanParams& p, int seq, int chunk, const float (&a)[8],
+                                               float (&sin_)[8]) {
+  const int lane = lane_id();
+  // Publishing: every lane stores its 8 channels, __syncwarp orders those stores
+  // before lane 0's release store of the flag (the release is cumulative over
+  // them), so no separate fence is needed.
+  const int64_t rec = (int64_t)seq * p.nchunks + chunk;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) sin_[c] = 0.f;
+  if (chunk == 0) {
+    float4* dst = reinterpret_cast<float4*>(p.inc + rec * kSlice + lane * 8);
+    __stcg(dst, make_float4(a[0], a[1], a[2], a[3]));
+    __stcg(dst + 1, make_float4(a[4], a[5], a[6], a[7]));
+    __syncwarp();
+    if (lane == 0) st_release_u32(p.flags + rec, kFlagInc);
+  } else {
+    {
+      float4* dst = reinterpret_cast<float4*>(p.agg + rec * kSlice + lane * 8);
+      __stcg(dst, make_float4(a[0], a[1], a[2], a[3]));
+      __stcg(dst + 1, make_float4(a[4], a[5], a[6], a[7]));
+      __syncwarp();
+      if (lane == 0) st_release_u32(p.flags + rec, kFlagAgg);
+    }
+    // Parallel look-back: lane l watches predecessor chunk (base - l); one
+    // round trip finds the nearest predecessor whose inclusive state is
+    // published (chunk -1 counts as an inclusive zero state), then the
+    // aggregates in between and that inclusive state are read together.
+    const uint32_t* seq_flags = p.flags + (int64_t)seq * p.nchunks;
+    const int64_t seq_rec = (int64_t)seq * p.nchunks;
+    int base = chunk - 1;  // nearest predecessor not yet accounted for
+    float mult = 1.f;      // beta^(64 * (chunk - 1 - base))
+    const uint64_t tstart = globaltimer_ns();
+    while (true) {
+      const int pc = base - lane;
+      const uint32_t f = pc >= 0 ? ld_acquire_u32(seq_flags + pc) : kFlagInc;
+      const uint32_t inc_mask = __ballot_sync(0xffffffffu, f == kFlagInc);
+      const uint32_t nil_mask = __ballot_sync(0xffffffffu, f == 0u);
+      const int l_inc = inc_mask ? __ffs(inc_mask) - 1 : 32;
+      const uint32_t needed = l_inc >= 32 ? 0xffffffffu : ((1u << l_inc) - 1u);
+      if (nil_mask & needed) {  // an aggregate on the way is not published yet
+        if (globaltimer_ns() - tstart > kWaitLimitNs) {
+          if (lane == 0) atomicOr(p.status, kStatusLookbackTimeout);
+          break;  // give up: the rest counts as zero
+        }
+        __nanosleep(32);
+        continue;
+      }
+      __syncwarp();  // orders the lanes' acquires before every lane's record reads
+      const int nk = l_inc >= 32 ? 32 : l_inc + 1;
+      for (int k = 0; k < nk; ++k) {
+        const int pck = base - k;
+        if (pck < 0) break;  // the zero state before the sequence
+        const float* src = (k == l_inc ? p.inc : p.agg) + (seq_rec + pck) * kSlice + lane * 8;
+        const float4 v0 = __ldcg(reinterpret_cast<const float4*>(src));
+        const float4 v1 = __ldcg(reinterpret_cast<const float4*>(src) + 1);
+        sin_[0] += mult * v0.x;
+        sin_[1] += mult * v0.y;
+        sin_[2] += mult * v0.z;
+        sin_[3] += mult * v0.w;
+        sin_[4] += mult * v1.x;
+        sin_[5] += mult * v1.y;
+        sin_[6] += mult * v1.z;
+        sin_[7] += mult * v1.w;
+        mult *= p.beta64;
+      }
+      if (l_inc < 32) break;
+      base -= 32;
+    }
+    float inc[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) inc[c] = a[c] + p.beta64 * sin_[c];
+    float4* dst = reinterpret_cast<float4*>(p.inc + rec * kSlice + lane * 8);
+    __stcg(dst, make_float4(inc[0], inc[1], inc[2], inc[3]));
+    __stcg(dst + 1, make_float4(inc[4], inc[5], inc[6], inc[7]));
+    __syncwarp();
+    if (lane == 0) st_release_u32(p.flags + rec, kFlagInc);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, FMKA_SCAN_MINB) route_ema_blend_kernel(const __grid_constant__ ScanParams p) {
   __shared__ uint32_t s_tile;
   __shared__ float s_wagg[kWarps][kSlice];
   __shared__ float s_in[kSlice];
@@ -185,69 +273,8 @@ __global__ void __launch_bounds__(kThreads, 2) route_ema_blend_kernel(const __gr
       for (int w = 0; w < kWarps; ++w) v = p.beta8 * v + s_wagg[w][lane * 8 + c];
       a[c] = v;
     }
-    const int64_t rec = (int64_t)seq * p.nchunks + chunk;
-    float sin_[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (chunk == 0) {
-      float4* dst = reinterpret_cast<float4*>(p.inc + rec * kSlice + lane * 8);
-      __stcg(dst, make_float4(a[0], a[1], a[2], a[3]));
-      __stcg(dst + 1, make_float4(a[4], a[5], a[6], a[7]));
-      __threadfence();
-      __syncwarp();
-      if (lane == 0) st_release_u32(p.flags + rec, kFlagInc);
-    } else {
-      {
-        float4* dst = reinterpret_cast<float4*>(p.agg + rec * kSlice + lane * 8);
-        __stcg(dst, make_float4(a[0], a[1], a[2], a[3]));
-        __stcg(dst + 1, make_float4(a[4], a[5], a[6], a[7]));
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) st_release_u32(p.flags + rec, kFlagAgg);
-      }
-      float mult = 1.f;
-      for (int pc = chunk - 1; pc >= 0; --pc) {
-        const int64_t prec = (int64_t)seq * p.nchunks + pc;
-        uint32_t f = 0;
-        if (lane == 0) {
-          f = ld_acquire_u32(p.flags + prec);
-          if (f == 0) {
-            const uint64_t tstart = globaltimer_ns();
-            while ((f = ld_acquire_u32(p.flags + prec)) == 0) {
-              __nanosleep(64);
-              if (globaltimer_ns() - tstart > kWaitLimitNs) {
-                atomicOr(p.status, kStatusLookbackTimeout);
-                f = 0xFFFFFFFFu;
-                break;
-              }
-            }
-          }
-        }
-        f = __shfl_sync(0xffffffffu, f, 0);
-        if (f == 0xFFFFFFFFu) break;  // timed out: treat the rest as zero
-        (void)ld_acquire_u32(p.flags + prec);  // per-lane acquire before reading the record
-        const float* src = (f == kFlagInc ? p.inc : p.agg) + prec * kSlice + lane * 8;
-        const float4 v0 = __ldcg(reinterpret_cast<const float4*>(src));
-        const float4 v1 = __ldcg(reinterpret_cast<const float4*>(src) + 1);
-        sin_[0] += mult * v0.x;
-        sin_[1] += mult * v0.y;
-        sin_[2] += mult * v0.z;
-        sin_[3] += mult * v0.w;
-        sin_[4] += mult * v1.x;
-        sin_[5] += mult * v1.y;
-        sin_[6] += mult * v1.z;
-        sin_[7] += mult * v1.w;
-        if (f == kFlagInc) break;
-        mult *= p.beta64;
-      }
-      float inc[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) inc[c] = a[c] + p.beta64 * sin_[c];
-      float4* dst = reinterpret_cast<float4*>(p.inc + rec * kSlice + lane * 8);
-      __stcg(dst, make_float4(inc[0], inc[1], inc[2], inc[3]));
-      __stcg(dst + 1, make_float4(inc[4], inc[5], inc[6], inc[7]));
-      __threadfence();
-      __syncwarp();
-      if (lane == 0) st_release_u32(p.flags + rec, kFlagInc);
-    }
+    float sin_[8];
+    chunk_lookback(p, seq, chunk, a, sin_);
 #pragma unroll
     for (int c = 0; c < 8; ++c) s_in[lane * 8 + c] = sin_[c];
   }
