@@ -418,6 +418,55 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_kernel_only(args):
+    """`--only KERNEL`: launches one kernel of the layer alone (warmup + steps
+    launches) on synthetic inputs of the configured shapes, with the batch
+    overridable by --batch: the small-case command for ncu captures."""
+    from mka_b200 import ops
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    c, d = PREFILL, DECODE
+    n = args.warmup + args.steps
+    if args.only in ("attn_prefill", "route_ema_blend", "qr_proj", "kv_proj", "o_proj"):
+        B = args.batch or c["B"]
+        T, D = c["T"], c["D"]
+        if args.only == "attn_prefill":
+            q = torch.randn(B, c["H"], T, 128, generator=g, device=dev, dtype=torch.bfloat16)
+            k = torch.randn(B, c["HKV"], T, 128, generator=g, device=dev, dtype=torch.bfloat16)
+            v = torch.randn(B, c["HKV"], T, 128, generator=g, device=dev, dtype=torch.bfloat16)
+            fn = lambda: ops.attn_prefill(q, k, v)  # noqa: E731
+        elif args.only == "route_ema_blend":
+            x = torch.randn(B, T, D, generator=g, device=dev, dtype=torch.bfloat16)
+            lg = torch.randn(B * T, c["L"], generator=g, device=dev)
+            fn = lambda: ops.route_ema_blend(x, 0.9, logits=lg, b2=None, levels=c["L"])  # noqa: E731
+        else:
+            layer = build_layer(c, dev)
+            W = layer.prepared(dev)
+            x = (torch.randn(B * T, D, generator=g, device=dev) / math.sqrt(D)).to(torch.bfloat16)
+            cos, sin = layer.rotary_emb.cos_sin(torch.arange(T, device=dev), dev)
+            if args.only == "qr_proj":
+                fn = lambda: ops.qr_proj(x, W.w_qr, W.b_qr, B, T, c["H"], W.router_hidden, W.w2, c["L"], W.act,  # noqa
+                                         rope=(cos, sin))
+            elif args.only == "kv_proj":
+                fn = lambda: ops.kv_proj(x, W.w_kv, W.b_kv, B, T, c["HKV"], rope=(cos, sin))  # noqa: E731
+            else:
+                fn = lambda: ops.gemm(x, W.w_o, W.b_o)  # noqa: E731
+    elif args.only == "attn_decode":
+        B = args.batch or d["B"]
+        q = torch.randn(B, d["H"], 1, 128, generator=g, device=dev, dtype=torch.bfloat16)
+        k = torch.randn(B, d["HKV"], d["TK"], 128, generator=g, device=dev, dtype=torch.bfloat16).mul_(0.1)
+        v = torch.randn(B, d["HKV"], d["TK"], 128, generator=g, device=dev, dtype=torch.bfloat16).mul_(0.1)
+        fn = lambda: ops.attn_decode(q, k, v)  # noqa: E731
+    else:
+        raise SystemExit(f"unknown kernel {args.only}")
+    for _ in range(n):
+        fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"only": args.only, "launches": n, "device_status": ops.device_status()}))
+
+
 def _config(args):
     c = PREFILL
     return {"workload": f"FastMKA attention layer prefill, Qwen-7B-like: batch {c['B']} per GPU, seq {c['T']}, "
@@ -435,7 +484,13 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", default=None,
+                    help="run one kernel alone (attn_prefill, attn_decode, route_ema_blend, qr_proj, kv_proj, o_proj)")
+    ap.add_argument("--batch", type=int, default=0, help="batch override for --only")
     args = ap.parse_args()
+    if args.only:
+        run_kernel_only(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return
