@@ -125,6 +125,23 @@ FMKA_API int fmka_route_ema_blend(const void* x, int64_t x_sb, int64_t x_st, con
                          int B, int T, int D, void* h, int64_t h_sb, int64_t h_st, float* lam, void* workspace,
                          size_t workspace_bytes, fmka_stream_t stream);
 
+/* fmka_route_ema_blend_noalloc: the same computation as fmka_route_ema_blend,
+ * for callers that cannot allocate device memory at call time (a runtime that
+ * reserved the whole GPU for its own pools, a real-time path that must not
+ * trigger cudaMalloc's synchronisation, a C program with no allocator). No
+ * counterpart in the reference. It allocates nothing: its scratch is a static
+ * device array of fmka_route_ema_blend_noalloc_scratch_bytes() (4 MiB) held by
+ * every GPU that loads the library, so shapes whose
+ * fmka_route_ema_blend_workspace_size() exceeds that are rejected with
+ * FMKA_ERR_UNSUPPORTED. The first call on a device looks up the array's device
+ * address (make it before any stream capture). All calls share the array:
+ * calls that overlap on the GPU race. */
+FMKA_API int fmka_route_ema_blend_noalloc(const void* x, int64_t x_sb, int64_t x_st, const float* logits,
+                                          const float* b2, const float* gate, int L, const void* l3, int64_t l3_sb,
+                                          int64_t l3_st, int T3, float beta, int B, int T, int D, void* h,
+                                          int64_t h_sb, int64_t h_st, float* lam, fmka_stream_t stream);
+FMKA_API size_t fmka_route_ema_blend_noalloc_scratch_bytes(void);
+
 /* Route blend with all three memories given (no scan):
  * H = gate0*l1 + gate1*l2 (+ gate2*l3), gate fp32 [B*T, L]. This is the blend
  * inside the reference's fused route kernel (mka/cuda/fused_route_mka.cu:60-67,

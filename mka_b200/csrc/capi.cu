@@ -23,6 +23,12 @@ int launch_route_ema_blend(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, c
                            int64_t l3_st, int T3, float beta, int B, int T, int D, __nv_bfloat16* h,
                            int64_t h_sb, int64_t h_st, float* lam, void* workspace, size_t workspace_bytes,
                            bool clear_flags, cudaStream_t stream);
+size_t route_ema_blend_static_scratch_bytes();
+int launch_route_ema_blend_static_scratch(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, const float* logits,
+                                          const float* b2, const float* gate, int L, const __nv_bfloat16* l3,
+                                          int64_t l3_sb, int64_t l3_st, int T3, float beta, int B, int T, int D,
+                                          __nv_bfloat16* h, int64_t h_sb, int64_t h_st, float* lam,
+                                          cudaStream_t stream);
 int launch_attn_prefill(const __nv_bfloat16* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
                         const __nv_bfloat16* k, const __nv_bfloat16* v, int64_t kv_sb, int64_t kv_sh,
                         int64_t kv_st, __nv_bfloat16* o, int64_t o_sb, int64_t o_st, int64_t o_sh, float* lse,
@@ -313,6 +319,18 @@ int fmka_route_ema_blend(const void* x, int64_t x_sb, int64_t x_st, const float*
                                 beta, B, T, D, bfw(h), h_sb, h_st, lam, workspace, workspace_bytes, true,
                                 as_stream(stream));
 }
+
+int fmka_route_ema_blend_noalloc(const void* x, int64_t x_sb, int64_t x_st, const float* logits, const float* b2,
+                                 const float* gate, int L, const void* l3, int64_t l3_sb, int64_t l3_st, int T3,
+                                 float beta, int B, int T, int D, void* h, int64_t h_sb, int64_t h_st, float* lam,
+                                 fmka_stream_t stream) {
+  if (x == nullptr || h == nullptr) return set_error(kErrInvalidArgument, "route_ema_blend_noalloc: null pointer");
+  if (!std::isfinite(beta)) return set_error(kErrInvalidArgument, "route_ema_blend_noalloc: beta must be finite");
+  return launch_route_ema_blend_static_scratch(bf(x), x_sb, x_st, logits, b2, gate, L, bf(l3), l3_sb, l3_st, T3, beta,
+                                               B, T, D, bfw(h), h_sb, h_st, lam, as_stream(stream));
+}
+
+size_t fmka_route_ema_blend_noalloc_scratch_bytes(void) { return route_ema_blend_static_scratch_bytes(); }
 
 int fmka_route_blend(const void* l1, int64_t l1_sb, int64_t l1_st, const void* l2, int64_t l2_sb, int64_t l2_st,
                      const void* l3, int64_t l3_sb, int64_t l3_st, int T3, const float* gate, int L, int B, int T,

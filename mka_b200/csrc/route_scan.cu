@@ -24,6 +24,8 @@
 // sets a status bit and the scan continues with a zero contribution. Four CTAs
 // share an SM (64 registers a thread) so that one CTA's look-back latency is
 // covered by the others' loads.
+#include <mutex>
+
 #include "fmka_internal.h"
 #include "ptx.cuh"
 
@@ -419,6 +421,66 @@ int launch_route_ema_blend(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, c
   if (grid > 0x7FFFFFFF) return set_error(kErrUnsupported, "route_ema_blend: problem too large");
   route_ema_blend_kernel<<<(unsigned)grid, kThreads, 0, stream>>>(p);
   return check_cuda(cudaGetLastError(), "route_ema_blend launch");
+}
+
+// ---------------------------------------------------------------------------
+// Scratch without allocation.
+//
+// Some callers cannot allocate device memory when they call into this library:
+// a serving runtime that reserved all of the GPU's memory for its own pools at
+// start-up, a real-time path where cudaMalloc's implicit synchronisation is not
+// acceptable, or a plain C program that links only this library and has no
+// allocator of its own. For them the scan's scratch (chunk ticket, look-back
+// flags and the per-chunk aggregate/inclusive states) lives in this fixed
+// device array instead of a caller-provided workspace. Every GPU that loads the
+// library holds the array until the process exits.
+//
+// In host code `g_route_scan_scratch` only names a host-side stand-in for the
+// symbol; the device address comes from cudaGetSymbolAddress, once per device,
+// with that device current (the first call on a device does it, so make that
+// first call before any stream capture). Every call shares the array and it
+// keeps the previous call's contents: the flag region is cleared by a memset on
+// the calling stream before each launch, and calls that overlap on the GPU (on
+// different streams) race on the array.
+// ---------------------------------------------------------------------------
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;  // 4 MiB
+static __device__ __align__(256) uint8_t g_route_scan_scratch[kStaticScratchBytes];
+
+namespace {
+std::mutex g_static_scratch_mu;
+void* g_static_scratch_dev[64] = {nullptr};
+}  // namespace
+
+size_t route_ema_blend_static_scratch_bytes() { return kStaticScratchBytes; }
+
+int launch_route_ema_blend_static_scratch(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, const float* logits,
+                                          const float* b2, const float* gate, int L, const __nv_bfloat16* l3,
+                                          int64_t l3_sb, int64_t l3_st, int T3, float beta, int B, int T, int D,
+                                          __nv_bfloat16* h, int64_t h_sb, int64_t h_st, float* lam,
+                                          cudaStream_t stream) {
+  if (B <= 0 || T <= 0 || D <= 0) return set_error(kErrInvalidArgument, "route_ema_blend_noalloc: empty shape");
+  const size_t need = route_ema_blend_workspace_bytes(B, T, D);
+  if (need > kStaticScratchBytes)
+    return set_error(kErrUnsupported, "route_ema_blend_noalloc: this shape needs " + std::to_string(need) +
+                                          " bytes of scratch, more than the " + std::to_string(kStaticScratchBytes) +
+                                          "-byte static array; use fmka_route_ema_blend with a workspace");
+  int dev = -1;
+  int rc = check_cuda(cudaGetDevice(&dev), "route_ema_blend_noalloc: current device");
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return set_error(kErrDevice, "route_ema_blend_noalloc: device index out of range");
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_static_scratch_mu);
+    if (g_static_scratch_dev[dev] == nullptr) {
+      void* ptr = nullptr;
+      rc = check_cuda(cudaGetSymbolAddress(&ptr, g_route_scan_scratch), "route_ema_blend_noalloc: scratch address");
+      if (rc) return rc;
+      g_static_scratch_dev[dev] = ptr;
+    }
+    scratch = g_static_scratch_dev[dev];
+  }
+  return launch_route_ema_blend(x, x_sb, x_st, nullptr, 0, 0, logits, b2, gate, L, l3, l3_sb, l3_st, T3, beta, B, T,
+                                D, h, h_sb, h_st, lam, scratch, kStaticScratchBytes, /*clear_flags=*/true, stream);
 }
 
 }  // namespace fmka
