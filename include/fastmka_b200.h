@@ -89,6 +89,16 @@ FMKA_API int fmka_num_sms(void);
 FMKA_API int fmka_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, const float* bias, void* c, int64_t ldc,
                    int M, int N, int K, fmka_stream_t stream);
 
+/* fmka_gemm_bf16_kblocked: the same GEMM with A stored as K / a_kblk blocks of
+ * [M, a_kblk] (row stride lda, blocks a_blk_stride elements apart): A[m, k] =
+ * block[k / a_kblk][m][k % a_kblk]. This reads an all-gathered attention output
+ * ([ranks, B*T, heads_per_rank*128]) as the o_proj input without a permute copy.
+ * a_kblk % 64 == 0 and K % a_kblk == 0. Replaces the o_proj call of the
+ * head-sharded layer (mka/hf/attention.py:194-195). */
+FMKA_API int fmka_gemm_bf16_kblocked(const void* a, int a_kblk, int64_t a_blk_stride, int64_t lda, const void* w,
+                                     int64_t ldw, const float* bias, void* c, int64_t ldc, int M, int N, int K,
+                                     fmka_stream_t stream);
+
 /* fmka_qr_proj: one GEMM over x[M = B*T, D] with the stacked weight
  * w_qr = [Wq ; W1 * Wq]  ([Nq + R, D]) and fp32 bias_qr ([Nq + R] or NULL).
  *   columns [0, Nq)      -> q in head-split layout [B, Hq, T, 128] at strides

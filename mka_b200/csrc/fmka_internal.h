@@ -59,6 +59,8 @@ struct GemmSeg {
 
 struct GemmParams {
   int M, N, K;
+  int a_kblk;            // > 0: A is stored as K / a_kblk blocks of [M, a_kblk]
+  int64_t a_blk_stride;  // element distance between those blocks
   int n_split;  // columns < n_split use seg[0], the rest seg[1]
   GemmSeg seg[2];
   uint32_t* status;

@@ -135,7 +135,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-          tma_load_2d(sA + stage * Cfg::kABytes, &tmA, &full[stage], kb * kBK, m0);
+          if (p.a_kblk > 0)  // A split along K into blocks of a_kblk columns (a gathered buffer)
+            tma_load_3d(sA + stage * Cfg::kABytes, &tmA, &full[stage], (kb * kBK) % p.a_kblk, m0,
+                        (kb * kBK) / p.a_kblk);
+          else
+            tma_load_2d(sA + stage * Cfg::kABytes, &tmA, &full[stage], kb * kBK, m0);
           tma_load_2d(sB + stage * Cfg::kBBytes, &tmB, &full[stage], kb * kBK, n0);
           ++issued;
           if (++stage == S) {
@@ -418,7 +422,17 @@ int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int
   }
 
   CUtensorMap tmA, tmB;
-  {
+  if (p.a_kblk > 0) {
+    // A[m, k] = A_blocks[k / a_kblk][m][k % a_kblk]: blocks of a_kblk columns, rows
+    // lda apart inside a block, blocks a_blk_stride elements apart.
+    if (p.a_kblk % kBK != 0 || p.K % p.a_kblk != 0 || p.a_blk_stride % 8 != 0)
+      return set_error(kErrInvalidArgument, "gemm: K blocks must be multiples of 64 columns that tile K");
+    uint64_t dims[3] = {(uint64_t)p.a_kblk, (uint64_t)p.M, (uint64_t)(p.K / p.a_kblk)};
+    uint64_t strides[2] = {(uint64_t)lda * 2, (uint64_t)p.a_blk_stride * 2};
+    uint32_t box[3] = {kBK, kBM, 1};
+    int rc = make_tmap_bf16(&tmA, A, 3, dims, strides, box, true);
+    if (rc) return rc;
+  } else {
     uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.M};
     uint64_t strides[1] = {(uint64_t)lda * 2};
     uint32_t box[2] = {kBK, kBM};

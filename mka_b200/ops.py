@@ -98,6 +98,27 @@ def gemm(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
     return out
 
 
+def gemm_kblocked(a_blocks: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[M, N] = A[M, K] @ w[N, K]^T where A is given as blocks a_blocks[j] = A[:, j*kb:(j+1)*kb]
+    (a_blocks: [K / kb, M, kb], e.g. an all-gathered attention output), read in place."""
+    _check_cuda(a_blocks, w)
+    _check_bf16(a_blocks, w)
+    if a_blocks.dim() != 3 or a_blocks.stride(2) != 1:
+        raise RuntimeError("gemm_kblocked: a_blocks must be [nblk, M, kb] with a contiguous last dimension")
+    nblk, M, kb = a_blocks.shape
+    K = nblk * kb
+    if w.shape[1] != K:
+        raise RuntimeError("gemm_kblocked: w must be [N, nblk * kb]")
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a_blocks.device)
+    b32 = _f32(bias)
+    _lib.call("fmka_gemm_bf16_kblocked", a_blocks.data_ptr(), kb, a_blocks.stride(0), a_blocks.stride(1),
+              w.data_ptr(), w.stride(0), _ptr(b32), out.data_ptr(), out.stride(0), M, N, K, _stream(a_blocks))
+    return out
+
+
 def qr_proj(x2d: torch.Tensor, w_qr: torch.Tensor, bias_qr: Optional[torch.Tensor], B: int, T: int,
             num_heads: int, router_hidden: int, w2: Optional[torch.Tensor], levels: int, act: int,
             rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,

@@ -171,3 +171,15 @@ def test_attn_decode(ops, B, Hq, Hkv, Tk, splits):
     assert ops.device_status() == 0
     assert _rel(o, ro.transpose(1, 2)) < 2e-2
     assert (lse - rlse[..., 0]).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("nblk,M,kb,N", [(2, 300, 896, 384), (4, 1024, 128, 512), (1, 77, 256, 256)])
+def test_gemm_kblocked(ops, nblk, M, kb, N):
+    """A given as blocks of columns (the all-gathered attention output of a head-sharded layer)."""
+    g = torch.Generator(device="cuda").manual_seed(nblk * M)
+    blocks = torch.randn(nblk, M, kb, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, nblk * kb, device="cuda", generator=g) / math.sqrt(nblk * kb)).bfloat16()
+    bias = torch.randn(N, device="cuda", generator=g)
+    out = ops.gemm_kblocked(blocks, w, bias)
+    a = blocks.permute(1, 0, 2).reshape(M, nblk * kb).float()
+    assert _rel(out, a @ w.float().t() + bias) < 1e-2

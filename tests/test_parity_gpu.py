@@ -245,3 +245,28 @@ def test_decode_llama_like_full_size_sampled_heads():
             assert abs(lse[b, hq].item() - torch.logsumexp(s, 0).item()) < TOL
             assert nrel(o[b, 0, hq], torch.softmax(s, 0) @ v[b, hq // 4].float()) < TOL
     assert ops.device_status() == 0
+
+
+def _hf_like_layer(seed=0, D=512, H=4, HKV=2, R=256):
+    """A Qwen2-like HF attention module (q/k/v bias, GQA) wrapped by HFFastMKAAttention, on cuda."""
+    from mka_b200 import HFFastMKAAttention
+
+    class _Attn(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.hidden_size, self.num_heads, self.num_key_value_heads = D, H, HKV
+            self.q_proj = nn.Linear(D, H * 128, bias=True)
+            self.k_proj = nn.Linear(D, HKV * 128, bias=True)
+            self.v_proj = nn.Linear(D, HKV * 128, bias=True)
+            self.o_proj = nn.Linear(H * 128, D, bias=False)
+
+    torch.manual_seed(seed)
+    layer = HFFastMKAAttention(_Attn(), use_l3=False)
+    layer.router = nn.Sequential(nn.Linear(D, R), nn.SiLU(), nn.Linear(R, 2))
+    with torch.no_grad():
+        for m in layer.modules():
+            if isinstance(m, nn.Linear):
+                m.weight.normal_(0, 0.04)
+                if m.bias is not None:
+                    m.bias.uniform_(-0.1, 0.1)
+    return layer.cuda().eval()

@@ -1,0 +1,67 @@
+"""Head-sharded FastMKA layer on 2 GPUs (NCCL): every rank's output for its
+sequences matches the unsharded layer run on the same sequences. Skipped with
+fewer than 2 GPUs."""
+import math
+import os
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _worker(rank, world, port, batch, q):
+    import torch.distributed as dist
+    import torch.nn as nn
+
+    from mka_b200 import ops
+    from mka_b200.layers.forward import fastmka_forward
+    from mka_b200.sharded import HeadShardedFastMKA, make_groups
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world)
+    try:
+        from tests.test_parity_gpu import _hf_like_layer
+
+        layer = _hf_like_layer(seed=3)
+        D, T = 512, 640
+        g = torch.Generator(device="cuda").manual_seed(17)
+        x_all = (torch.randn(batch, T, D, generator=g, device="cuda") / math.sqrt(D)).bfloat16()
+        pos = torch.arange(T, device="cuda").float()
+        inv = 1.0 / (10000 ** (torch.arange(0, 128, 2, device="cuda").float() / 128))
+        ang = torch.cat([pos[:, None] * inv, pos[:, None] * inv], -1)
+        rope = (ang.cos()[None], ang.sin()[None])
+        groups = make_groups(batch, layer.num_key_value_heads, world)
+        sh = HeadShardedFastMKA(layer, batch, rank, world, groups)
+        b0, b1 = sh.plan.batch
+        out = sh(x_all[b0:b1].contiguous(), rope=rope)
+        ref = fastmka_forward(x_all[b0:b1].contiguous(), layer.prepared(torch.device("cuda")), layer.num_heads,
+                              layer.num_key_value_heads, layer.ema_beta, False, rope=rope)["out"]
+        torch.cuda.synchronize()
+        err = ((out.float() - ref.float()).abs().max() / ref.float().abs().max()).item()
+        q.put((rank, err, len(sh.plan.group), ops.device_status()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("batch", [1, 2])
+def test_head_sharded_layer_matches_unsharded(batch):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29100 + batch + os.getpid() % 500
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, batch, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=180) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, err, gsize, status in res:
+        assert status == 0
+        assert gsize == (2 if batch == 1 else 1)
+        assert err < 2e-2
