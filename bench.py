@@ -44,6 +44,7 @@ sys.path.insert(0, ROOT)
 
 PREFILL = dict(B=4, T=8192, D=3584, H=28, HKV=4, R=512, L=2, theta=1.0e6, bias=True)
 DECODE = dict(B=64, TK=32768, D=4096, H=32, HKV=8, R=2048, L=2, theta=5.0e5, bias=False)
+LONG = dict(B=2, T=32768, D=3584, H=28, HKV=4, R=512, L=3, theta=1.0e6, bias=True)
 CPU_SAMPLE_T = 2048  # CPU sample: the first 2048 tokens of one prefill sequence
 
 
@@ -345,6 +346,62 @@ def bench_decode(args, dist, rank, world, device, peaks):
     }
 
 
+# ------------------------------------------------------------ long context --
+def bench_long_context(args, dist, rank, world, device, peaks):
+    """The Qwen-7B-like layer with L3 retrieved memory at batch 2, seq 32768 (fixed
+    total work): whole sequences per rank up to 2 GPUs, then kv heads split inside
+    each sequence's group with one NCCL all-gather before o_proj."""
+    from mka_b200.sharded import HeadShardedFastMKA, make_groups
+
+    c = LONG
+    B, T, D = c["B"], c["T"], c["D"]
+    layer = build_layer(c, device, seed=2)
+    groups = make_groups(B, c["HKV"], world) if dist is not None else {}
+    sh = HeadShardedFastMKA(layer, B, rank, world, groups)
+    b0, b1 = sh.plan.batch
+    g = torch.Generator(device=device).manual_seed(3000)
+    x = (torch.randn(B, T, D, generator=g, device=device) / math.sqrt(D)).to(torch.bfloat16)[b0:b1].contiguous()
+    r = (torch.randn(B, T, D, generator=g, device=device) * 0.5).to(torch.bfloat16)[b0:b1].contiguous()
+    cos, sin = layer.rotary_emb.cos_sin(torch.arange(T, device=device), device)
+    pe = (cos, sin)
+
+    def step():
+        sh(x, rope=pe, l3_memory=r)
+
+    for _ in range(max(2, args.warmup)):
+        step()
+    steps = max(3, min(args.steps, 10))
+    ms = _timed(dist, step, steps)
+    # this rank's attention kernel alone: its query heads over its sequences
+    from mka_b200 import ops
+
+    h0, h1 = sh.plan.kv_heads
+    hq = (h1 - h0) * (c["H"] // c["HKV"])
+    q = torch.randn(b1 - b0, hq, T, 128, generator=g, device=device, dtype=torch.bfloat16)
+    k = torch.randn(b1 - b0, h1 - h0, T, 128, generator=g, device=device, dtype=torch.bfloat16)
+    v = torch.randn_like(k)
+    for _ in range(2):
+        ops.attn_prefill(q, k, v, want_lse=False)
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        ops.attn_prefill(q, k, v, want_lse=False)
+    e.record()
+    torch.cuda.synchronize()
+    attn_ms = a.elapsed_time(e) / steps
+    flops = 4.0 * (b1 - b0) * hq * 128 * T * (T + 1) / 2
+    achieved = flops / (attn_ms * 1e-3) / 1e12
+    return {"metric": "FastMKA prefill tokens/s, long context with L3 (fixed total work)",
+            "value": B * T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "scaling": "strong",
+            "config": {"batch": B, "seq_len": T, "d_model": D, "heads": f"{c['H']}/{c['HKV']}", "levels": 3,
+                       "router": f"{D}->{c['R']}->3", "partition": f"sequences x kv heads, group size "
+                                                                  f"{len(sh.plan.group)}"},
+            "roofline": {"bound": "tensor", "kernel": "attn_prefill (this rank's heads, T=32768)",
+                         "achieved": round(achieved, 1), "peak": peaks["bf16"], "unit": "TFLOP/s",
+                         "frac": round(achieved / peaks["bf16"], 4), "peak_kind": f"{peaks['src']} burst bf16",
+                         "launch_ms": attn_ms}}
+
+
 # -------------------------------------------------------------- CPU (oracle) --
 def _oracle_params(layer):
     f = lambda t: None if t is None else t.detach().float().cpu()  # noqa: E731
@@ -484,6 +541,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-long", action="store_true", help="skip the long-context (L3, seq 32768) measurement")
     ap.add_argument("--only", default=None,
                     help="run one kernel alone (attn_prefill, attn_decode, route_ema_blend, qr_proj, kv_proj, o_proj)")
     ap.add_argument("--batch", type=int, default=0, help="batch override for --only")
@@ -504,6 +562,15 @@ def main():
     sampler.start()
     pre = bench_prefill(args, dist, rank, world, device, peaks)
     dec = None if args.no_decode else bench_decode(args, dist, rank, world, device, peaks)
+    lc = None
+    if not args.no_long:
+        try:
+            from mka_b200.sharded import plan_units
+
+            plan_units(LONG["B"], LONG["HKV"], world)  # raises for world sizes the units do not split over
+            lc = bench_long_context(args, dist, rank, world, device, peaks)
+        except ValueError as e:
+            lc = {"skipped": str(e)}
     clocks = sampler.stop()
     status = ops.device_status()
     cpu = None
@@ -537,6 +604,8 @@ def main():
                            "heads": f"{d['H']}/{d['HKV']}"},
                 "gpu_launches": launches_per_step * args.steps,
             }
+        if lc is not None:
+            line["long_context"] = lc
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
