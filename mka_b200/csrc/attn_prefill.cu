@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], 4);  // one arrival per softmax warp
       mbar_init(&o_full[i], 1);
     }
     for (int s = 0; s < kKS; ++s) {
@@ -409,7 +409,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       z = z * alpha + (asum.x + asum.y);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[ti]);
+      __syncwarp();  // every lane's P store has completed (wait::st) before the warp's arrival
+      if (lane == 0) mbar_arrive(&p_full[ti]);
     }
     if (!ok) *abort_flag = 1;
     // ---- epilogue: O / z and LSE ----

@@ -101,7 +101,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -382,7 +382,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      __syncwarp();  // every lane's TMEM reads have completed before the warp's arrival
+      if (lane == 0) mbar_arrive(&tempty[acc]);
     }
   }
 
