@@ -215,43 +215,53 @@ def _traffic(name):
 
 
 def _e2e_pipelined(dist, layer, x, pe, steps):
-    """Average ms per step of host->device input, forward, device->host output,
-    with the copies of neighbouring steps overlapping the compute (device-timed on
-    the compute stream, which waits for the last download before the end event)."""
+    """Average ms per step of host->device input, forward, device->host output.
+
+    Each step's sequences are pipelined as separate units through the public
+    layer call: the upload of unit u+1 and the download of unit u-1 overlap the
+    forward of unit u on three streams, so only one sequence's upload and one
+    sequence's download are not hidden. Device-timed on the compute stream,
+    which waits for the last download before the end event."""
     comp = torch.cuda.current_stream()
     up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    B = x.shape[0]
     g = torch.Generator().manual_seed(7)
     x_host = [x.cpu().pin_memory(), (x.cpu() + 0.01 * torch.randn(x.shape, generator=g).to(x.dtype)).pin_memory()]
     out_host = [torch.empty(x.shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    x_dev = [torch.empty_like(x), torch.empty_like(x)]
-    ev_up = [torch.cuda.Event(), torch.cuda.Event()]
-    ev_comp = [torch.cuda.Event(), torch.cuda.Event()]
+    nbuf = 3
+    x_dev = [torch.empty_like(x[:1]) for _ in range(nbuf)]
+    ev_up = [torch.cuda.Event() for _ in range(nbuf)]
+    ev_comp = [torch.cuda.Event() for _ in range(nbuf)]
 
-    def run(n):
+    def unit_src(u):
+        return x_host[(u // B) % 2][u % B: u % B + 1]
+
+    def run(n_steps):
+        n = n_steps * B
         with torch.cuda.stream(up):
-            x_dev[0].copy_(x_host[0], non_blocking=True)
+            x_dev[0].copy_(unit_src(0), non_blocking=True)
             ev_up[0].record(up)
         last_down = torch.cuda.Event()
-        for i in range(n):
-            b = i % 2
-            if i + 1 < n:
-                nb = (i + 1) % 2
+        for u in range(n):
+            bu = u % nbuf
+            if u + 1 < n:
+                nb = (u + 1) % nbuf
                 with torch.cuda.stream(up):
-                    if i >= 1:
-                        up.wait_event(ev_comp[nb])  # step i-1 has finished reading that buffer
-                    x_dev[nb].copy_(x_host[nb], non_blocking=True)
+                    if u + 1 >= nbuf:
+                        up.wait_event(ev_comp[nb])  # the unit that last used this buffer has been read
+                    x_dev[nb].copy_(unit_src(u + 1), non_blocking=True)
                     ev_up[nb].record(up)
-            comp.wait_event(ev_up[b])
-            out, _, _ = layer(x_dev[b], position_embeddings=pe)
-            ev_comp[b].record(comp)
+            comp.wait_event(ev_up[bu])
+            out, _, _ = layer(x_dev[bu], position_embeddings=pe)
+            ev_comp[bu].record(comp)
             with torch.cuda.stream(down):
-                down.wait_event(ev_comp[b])
-                out_host[b].copy_(out, non_blocking=True)
+                down.wait_event(ev_comp[bu])
+                out_host[(u // B) % 2][u % B: u % B + 1].copy_(out, non_blocking=True)
                 out.record_stream(down)
                 last_down.record(down)
         comp.wait_event(last_down)
 
-    run(3)
+    run(2)
     _barrier(dist)
     a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(comp)
@@ -290,8 +300,8 @@ def bench_prefill(args, dist, rank, world, device, peaks):
 
     # end to end through the module with host buffers: every step uploads its
     # input from pinned host memory and downloads the layer output, pipelined
-    # across steps on three streams (upload of step i+1 and download of step
-    # i-1 overlap the compute of step i), with double-buffered device tensors
+    # per sequence on three streams (the upload of the next sequence and the
+    # download of the previous one overlap the forward of the current one)
     e2e_ms = _e2e_pipelined(dist, layer, x, pe, args.steps)
     tokens = B * T * world
     return {
@@ -586,7 +596,7 @@ def main():
             "config": _config(args),
             "e2e": {"value": pre["e2e_tok_s"], "unit": "tokens/s", "h2d_bytes_per_step": pre["h2d"],
                     "d2h_bytes_per_step": pre["d2h"], "ms_per_step": pre["e2e_ms"],
-                    "pipeline": "upload of step i+1 and download of step i-1 overlap step i (3 streams)"},
+                    "pipeline": "per sequence: upload of sequence u+1 and download of u-1 overlap the forward of u (3 streams)"},
             "roofline": pre["roofline"],
             "cpu_baseline": cpu,
             "gpu_launches": launches_per_step * args.steps,
