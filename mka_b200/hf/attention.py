@@ -14,7 +14,16 @@ Extensions: `l3_memory` ([B, T3, D]) feeds a per-position L3 level when
 use_l3 is set (the reference always blends zeros, hf/attention.py:100-102);
 the head counts are read from the wrapped module's config when the module no
 longer carries them (transformers >= 4.48); a `StaticKVCache` passed as
-past_key_value is written in place instead of concatenated.
+past_key_value is written in place instead of concatenated; a transformers
+Cache object (past_key_values of transformers >= 4.48: anything with
+update(k, v, layer_idx)) receives the new post-RoPE k/v through its own
+update and the layer attends to what it returns; `return_present=False`
+gives the two-value return (attn_output, attn_weights) that the decoder
+layers of transformers >= 4.48 unpack, and with it RoPE follows that
+version's contract (position_embeddings from the model, no rotary_emb on the
+module). Additive masks are not supported
+(causal only): with the default sdpa attention implementation transformers
+passes no mask for unpadded prefill and cached decode.
 """
 from __future__ import annotations
 
@@ -38,8 +47,10 @@ def _attr(mod: nn.Module, name: str, cfg_name: str, default=None):
 
 class HFFastMKAAttention(nn.Module):
     def __init__(self, original_attn: nn.Module, use_l3: bool = False, ema_beta: float = 0.9,
-                 use_cuda_kernel: bool = True, prefer_sdpa: bool = True):
+                 use_cuda_kernel: bool = True, prefer_sdpa: bool = True, return_present: bool = True):
         super().__init__()
+        self.return_present = return_present
+        self.layer_idx = getattr(original_attn, "layer_idx", None)
         self.original_attn = original_attn
         self.use_l3 = use_l3
         self.ema_beta = ema_beta
@@ -91,10 +102,22 @@ class HFFastMKAAttention(nn.Module):
                 rope = position_embeddings
             else:
                 rope = self.rotary_emb(hidden_states, position_ids)
+        elif not self.return_present and position_embeddings is not None:
+            # transformers >= 4.48: the model computes (cos, sin) once and the
+            # attention modules no longer carry rotary_emb
+            rope = position_embeddings
         dt = hidden_states.dtype
         W = self.prepared(hidden_states.device)
         with torch.no_grad():
-            if isinstance(past_key_value, StaticKVCache):
+            if _is_hf_cache(past_key_value):
+                if self.layer_idx is None:
+                    raise RuntimeError("a transformers Cache needs the wrapped attention's layer_idx")
+                cache, idx = past_key_value, self.layer_idx
+                r = fastmka_forward(hidden_states, W, self.num_heads, self.num_key_value_heads, self.ema_beta,
+                                    self.use_l3, l3_memory=l3_memory, rope=rope,
+                                    kv_update=lambda k, v: cache.update(k, v, idx))
+                present = None  # the Cache object holds them
+            elif isinstance(past_key_value, StaticKVCache):
                 cache = past_key_value
                 kc, vc = cache.layer(self)
                 r = fastmka_forward(hidden_states, W, self.num_heads, self.num_key_value_heads, self.ema_beta,
@@ -120,4 +143,12 @@ class HFFastMKAAttention(nn.Module):
         out, w, present, _, _ = self.forward_with_lse(hidden_states, attention_mask, position_ids, past_key_value,
                                                       output_attentions, use_cache, cache_position,
                                                       position_embeddings, **kwargs)
+        if not self.return_present:
+            return out, w
         return out, w, present
+
+
+def _is_hf_cache(obj) -> bool:
+    """A transformers Cache (DynamicCache, StaticCache, ...): has update(k, v, layer_idx)."""
+    return (obj is not None and not isinstance(obj, (tuple, list, StaticKVCache))
+            and callable(getattr(obj, "update", None)))

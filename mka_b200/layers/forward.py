@@ -16,7 +16,7 @@ Reference: mka/layers/fastmka.py:71-177 and mka/hf/attention.py:82-199.
 """
 from __future__ import annotations
 
-from typing import Optional, Tuple
+from typing import Callable, Optional, Tuple
 
 import torch
 
@@ -31,7 +31,9 @@ def fastmka_forward(x: torch.Tensor, W: PreparedWeights, num_heads: int, num_kv_
                     past: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
                     rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
                     kv_out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
-                    past_len: Optional[int] = None, timers: Optional[list] = None) -> dict:
+                    past_len: Optional[int] = None, timers: Optional[list] = None,
+                    kv_update: Optional[Callable[[torch.Tensor, torch.Tensor],
+                                                 Tuple[torch.Tensor, torch.Tensor]]] = None) -> dict:
     """Runs the layer on x [B, T, D] (any float dtype; computed in bf16).
 
     past:    (k, v) [B, Hkv, Tp, 128] cached keys/values; the returned k/v are
@@ -42,6 +44,9 @@ def fastmka_forward(x: torch.Tensor, W: PreparedWeights, num_heads: int, num_kv_
              valid prefix (no copy of the cache).
     timers:  if a list is given, (stage, start_event, end_event) CUDA event
              pairs recorded on the current stream around each launch are appended.
+    kv_update: alternatively a callable given this call's new (k, v)
+             [B, Hkv, T, 128] (post-RoPE) that returns the full (k, v) to attend
+             to, e.g. a transformers Cache's update(k, v, layer_idx).
     Returns dict(out [B,T,D] bf16, k, v, lam [B,T,L] fp32, lse).
     """
     def mark(name):
@@ -107,6 +112,10 @@ def fastmka_forward(x: torch.Tensor, W: PreparedWeights, num_heads: int, num_kv_
                     t_offset=tp)
     else:
         k_tot, v_tot = ops.kv_proj(h.view(B * T, D), W.w_kv, W.b_kv, B, T, num_kv_heads, rope=rope)
+        if kv_update is not None:
+            k_tot, v_tot = kv_update(k_tot, v_tot)
+            if k_tot.dtype != torch.bfloat16 or v_tot.dtype != torch.bfloat16:
+                raise RuntimeError("the K/V returned by kv_update must be bf16")
     done()
     # 4. attention
     mark("attention")

@@ -1,0 +1,122 @@
+"""A transformers LlamaForCausalLM with the FastMKA self_attn patch installed,
+run the way transformers >= 4.48 runs it (decoder layers unpack two values,
+K/V go through a DynamicCache, RoPE comes in as position_embeddings), against
+the same model whose attention is the oracle in fp32 on the CPU.
+
+Reference behaviour: mka/hf/patch.py:30-48 (the patch), mka/hf/attention.py:82-199
+(the wrapped forward). Both models hold the same bf16-rounded weights; the
+patched one runs on cuda:0 in bf16.
+"""
+import copy
+
+import pytest
+import torch
+import torch.nn as nn
+
+transformers = pytest.importorskip("transformers")
+from transformers import DynamicCache, LlamaConfig, LlamaForCausalLM  # noqa: E402
+
+from mka_b200.hf.attention import HFFastMKAAttention, _is_hf_cache  # noqa: E402
+from mka_b200.hf.patch import HFPatchConfig, _two_value_attention_api, apply_hf_attention_patch  # noqa: E402
+from oracle import fastmka_oracle as O  # noqa: E402
+
+
+class OracleAttention(nn.Module):
+    """The reference HF FastMKA attention in fp32 on the CPU, with the weights of
+    a patched module, speaking the transformers >= 4.48 self_attn protocol."""
+
+    def __init__(self, patched: HFFastMKAAttention, layer_idx: int):
+        super().__init__()
+        f = lambda t: None if t is None else t.detach().float().cpu().clone()  # noqa: E731
+        self.p = {"wq": f(patched.q_proj.weight), "bq": f(patched.q_proj.bias),
+                  "wk": f(patched.k_proj.weight), "bk": f(patched.k_proj.bias),
+                  "wv": f(patched.v_proj.weight), "bv": f(patched.v_proj.bias),
+                  "wo": f(patched.o_proj.weight), "bo": f(patched.o_proj.bias),
+                  "r1w": f(patched.router[0].weight), "r1b": f(patched.router[0].bias),
+                  "r2w": f(patched.router[2].weight), "r2b": f(patched.router[2].bias)}
+        self.p = {k: v for k, v in self.p.items() if v is not None}
+        self.nh, self.nkv, self.beta = patched.num_heads, patched.num_key_value_heads, patched.ema_beta
+        self.idx = layer_idx
+
+    def forward(self, hidden_states, position_embeddings=None, attention_mask=None, past_key_values=None, **kw):
+        assert attention_mask is None
+        cos, sin = position_embeddings
+        past = None
+        if past_key_values is not None and past_key_values.get_seq_length(self.idx) > 0:
+            lay = past_key_values.layers[self.idx]
+            past = (lay.keys, lay.values)
+        r = O.hf_fastmka_forward(hidden_states.float(), self.p, self.nh, self.nkv, False, self.beta, "silu",
+                                 past=past, cos=cos.float().unsqueeze(1), sin=sin.float().unsqueeze(1))
+        if past_key_values is not None:
+            t = hidden_states.shape[1]
+            past_key_values.update(r["k"][:, :, -t:], r["v"][:, :, -t:], self.idx)
+        return r["out"], None
+
+
+def _tiny_llama(seed=0):
+    cfg = LlamaConfig(vocab_size=128, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                      num_attention_heads=2, num_key_value_heads=1, max_position_embeddings=1024,
+                      rope_theta=500000.0, attn_implementation="sdpa")
+    torch.manual_seed(seed)
+    return LlamaForCausalLM(cfg).eval()
+
+
+def _rel(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    return ((a - b).norm() / b.norm()).item()
+
+
+def test_patch_picks_transformers_protocol():
+    """Host logic only: the patch installs two-value modules on transformers
+    >= 4.48, leaves the reference's three-value form otherwise, and the Cache
+    detection accepts transformers caches but not tuples."""
+    model = _tiny_llama()
+    n = apply_hf_attention_patch(model, HFPatchConfig(verbose=False))
+    assert n == 2
+    for layer in model.model.layers:
+        assert isinstance(layer.self_attn, HFFastMKAAttention)
+        assert layer.self_attn.return_present == (not _two_value_attention_api())
+        assert layer.self_attn.layer_idx is not None
+    assert _is_hf_cache(DynamicCache())
+    assert not _is_hf_cache((torch.zeros(1), torch.zeros(1)))
+    assert not _is_hf_cache(None)
+    assert apply_hf_attention_patch(_tiny_llama(), HFPatchConfig(enabled=False, verbose=False)) == 0
+
+
+@pytest.mark.gpu
+def test_patched_llama_prefill_and_cached_decode():
+    if not _two_value_attention_api():
+        pytest.skip("needs the transformers >= 4.48 self_attn protocol")
+    model = _tiny_llama().to(torch.bfloat16)
+    assert apply_hf_attention_patch(model, HFPatchConfig(verbose=False)) == 2
+    with torch.no_grad():  # bf16-round the new router weights too, then copy for the oracle
+        for layer in model.model.layers:
+            for prm in layer.self_attn.router.parameters():
+                prm.copy_(prm.to(torch.bfloat16))
+    ref = copy.deepcopy(model).float()
+    for i, (lr, lm) in enumerate(zip(ref.model.layers, model.model.layers)):
+        lr.self_attn = OracleAttention(lm.self_attn, i)
+    model = model.to("cuda")
+
+    g = torch.Generator().manual_seed(1)
+    ids = torch.randint(0, 128, (2, 96), generator=g)
+    with torch.no_grad():
+        out = model(ids.cuda(), use_cache=True)
+        ref_out = ref(ids, use_cache=True)
+        assert isinstance(out.past_key_values, DynamicCache)
+        assert out.past_key_values.get_seq_length() == 96
+        # bf16 weights, activations, P and O against fp32 throughout: relative
+        # Frobenius error of the logits
+        assert _rel(out.logits, ref_out.logits) < 3e-2
+        pkv, rkv = out.past_key_values, ref_out.past_key_values
+        for step in range(2):
+            tok = torch.randint(0, 128, (2, 1), generator=g)
+            o = model(tok.cuda(), past_key_values=pkv, use_cache=True)
+            r = ref(tok, past_key_values=rkv, use_cache=True)
+            assert o.past_key_values.get_seq_length() == 97 + step
+            assert _rel(o.logits, r.logits) < 3e-2, step
+            pkv, rkv = o.past_key_values, r.past_key_values
+        k_gpu = pkv.layers[1].keys.float().cpu()
+        k_ref = rkv.layers[1].keys
+        assert k_gpu.shape == k_ref.shape == (2, 1, 98, 128)
+        assert _rel(k_gpu, k_ref) < 3e-2
