@@ -543,6 +543,74 @@ def _config(args):
             "l2": "inputs larger than L2 (X 235 MB per GPU; decode cache 8.6 GB)"}
 
 
+# -------------------------------------------------------------- full model --
+MODEL = dict(name="Llama-3-8B", vocab=128256, D=4096, FFN=14336, layers=32, H=32, HKV=8, theta=5e5, T=65536, B=1)
+
+
+def bench_model(args, device):
+    """The whole Llama-3-8B architecture from transformers (random bf16 weights,
+    N(0, 0.02)) with every self_attn replaced by the FastMKA module through the
+    reference's patch API, one prefill forward of a 65536-token sequence per
+    step (logits of the last position only). Also times one patched self_attn
+    alone at that length, the part of each layer this package replaces."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from mka_b200.hf.patch import HFPatchConfig, apply_hf_attention_patch
+
+    c = MODEL
+    cfg = LlamaConfig(vocab_size=c["vocab"], hidden_size=c["D"], intermediate_size=c["FFN"],
+                      num_hidden_layers=c["layers"], num_attention_heads=c["H"], num_key_value_heads=c["HKV"],
+                      max_position_embeddings=131072, rope_theta=c["theta"], attn_implementation="sdpa")
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(device):
+            torch.manual_seed(5)
+            model = LlamaForCausalLM(cfg).eval()
+            patched = apply_hf_attention_patch(model, HFPatchConfig(verbose=False))
+    finally:
+        torch.set_default_dtype(prev)
+    g = torch.Generator(device=device).manual_seed(6)
+    ids = torch.randint(0, c["vocab"], (c["B"], c["T"]), generator=g, device=device)
+
+    def step():
+        with torch.no_grad():
+            model(ids, use_cache=False, logits_to_keep=1)
+
+    step()  # warm-up: first call also folds and caches each layer's weights
+    steps = max(1, min(args.steps, 3))
+    ms = _timed(None, step, steps)
+
+    x = (torch.randn(c["B"], c["T"], c["D"], generator=g, device=device) * 0.5).to(torch.bfloat16)
+    pos = torch.arange(c["T"], device=device).unsqueeze(0)
+    pe = model.model.rotary_emb(x, pos)
+    attn = model.model.layers[0].self_attn
+
+    def attn_step():
+        with torch.no_grad():
+            attn(hidden_states=x, position_embeddings=pe)
+
+    attn_step()
+    attn_ms = _timed(None, attn_step, steps)
+    tokens = c["B"] * c["T"]
+    attn_flops = 4.0 * c["B"] * c["H"] * 128 * c["T"] * (c["T"] + 1) / 2
+    out = {
+        "metric": "Llama-3-8B prefill tokens/s, every self_attn patched with FastMKA (transformers model)",
+        "value": tokens / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+        "patched_layers": patched,
+        "fastmka_self_attn_ms_per_layer": attn_ms,
+        "fastmka_self_attn_share": round(attn_ms * c["layers"] / ms, 4),
+        "attention_tflops_per_layer": attn_flops / 1e12,
+        "config": {"model": c["name"], "layers": c["layers"], "d_model": c["D"], "ffn": c["FFN"],
+                   "heads": f"{c['H']}/{c['HKV']}", "vocab": c["vocab"], "rope_theta": c["theta"],
+                   "batch": c["B"], "seq_len": c["T"], "logits": "last position"},
+        "data": "synthetic token ids U[0, vocab), random N(0, 0.02) bf16 weights",
+    }
+    del model
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -552,6 +620,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-long", action="store_true", help="skip the long-context (L3, seq 32768) measurement")
+    ap.add_argument("--no-model", action="store_true",
+                    help="skip the full Llama-3-8B model measurement (one GPU only)")
     ap.add_argument("--only", default=None,
                     help="run one kernel alone (attn_prefill, attn_decode, route_ema_blend, qr_proj, kv_proj, o_proj)")
     ap.add_argument("--batch", type=int, default=0, help="batch override for --only")
@@ -582,6 +652,12 @@ def main():
         except ValueError as e:
             lc = {"skipped": str(e)}
     clocks = sampler.stop()
+    model = None
+    if not args.no_model:
+        if world == 1:
+            model = bench_model(args, device)
+        else:
+            model = {"skipped": "the full-model line runs on one GPU (its FFN and embeddings are not sharded)"}
     status = ops.device_status()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -616,6 +692,8 @@ def main():
             }
         if lc is not None:
             line["long_context"] = lc
+        if model is not None:
+            line["model"] = model
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
