@@ -21,7 +21,9 @@
  *                           softmax and the route blend
  *                           (mka/layers/session_memory.py:6-39;
  *                            mka/layers/fastmka.py:82-96; mka/hf/attention.py:97-107)
- *   fmka_kv_proj            k/v projection of the fused memory (+ RoPE on k)
+ *   fmka_route_ema_blend_state  the same with the EMA state carried across calls
+ *                           (extends session_memory.py:6-22, which restarts at zero)
+ *   fmka_kv_proj           k/v projection of the fused memory (+ RoPE on k)
  *                           (mka/layers/fastmka.py:98-99; mka/hf/attention.py:110-119)
  *   fmka_attn_fwd_prefill   causal attention: fastmka_attn (mka/cuda/ops.py:73,
  *                           mka/cuda/fastmka_attn.cpp:11-17, fastmka_attn.cu:133-172)
@@ -151,6 +153,20 @@ FMKA_API int fmka_route_ema_blend_noalloc(const void* x, int64_t x_sb, int64_t x
                                           int64_t l3_st, int T3, float beta, int B, int T, int D, void* h,
                                           int64_t h_sb, int64_t h_st, float* lam, fmka_stream_t stream);
 FMKA_API size_t fmka_route_ema_blend_noalloc_scratch_bytes(void);
+
+/* fmka_route_ema_blend_state: fmka_route_ema_blend with the EMA carried across
+ * calls. It extends causal_prefix_ema (mka/layers/session_memory.py:6-22),
+ * whose state starts at zero on every call (:17-21), with an initial state:
+ * L2[t] = beta * L2[t-1] + (1 - beta) * x[t] with L2[-1] = ema_init (fp32
+ * [B, D], contiguous; NULL = zero, which is fmka_route_ema_blend). ema_final
+ * (fp32 [B, D], may be NULL) receives L2[T-1], the state to pass to the next
+ * call; it must not alias ema_init. Both 16-byte aligned. */
+FMKA_API int fmka_route_ema_blend_state(const void* x, int64_t x_sb, int64_t x_st, const float* logits,
+                                        const float* b2, const float* gate, int L, const void* l3, int64_t l3_sb,
+                                        int64_t l3_st, int T3, float beta, int B, int T, int D, void* h,
+                                        int64_t h_sb, int64_t h_st, float* lam, const float* ema_init,
+                                        float* ema_final, void* workspace, size_t workspace_bytes,
+                                        fmka_stream_t stream);
 
 /* Route blend with all three memories given (no scan):
  * H = gate0*l1 + gate1*l2 (+ gate2*l3), gate fp32 [B*T, L]. This is the blend

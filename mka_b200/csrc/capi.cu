@@ -22,7 +22,8 @@ int launch_route_ema_blend(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, c
                            const float* b2, const float* gate, int L, const __nv_bfloat16* l3, int64_t l3_sb,
                            int64_t l3_st, int T3, float beta, int B, int T, int D, __nv_bfloat16* h,
                            int64_t h_sb, int64_t h_st, float* lam, void* workspace, size_t workspace_bytes,
-                           bool clear_flags, cudaStream_t stream);
+                           bool clear_flags, cudaStream_t stream, const float* ema_init = nullptr,
+                           float* ema_final = nullptr);
 size_t route_ema_blend_static_scratch_bytes();
 int launch_route_ema_blend_static_scratch(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, const float* logits,
                                           const float* b2, const float* gate, int L, const __nv_bfloat16* l3,
@@ -356,6 +357,20 @@ int fmka_route_ema_blend_noalloc(const void* x, int64_t x_sb, int64_t x_st, cons
 }
 
 size_t fmka_route_ema_blend_noalloc_scratch_bytes(void) { return route_ema_blend_static_scratch_bytes(); }
+
+int fmka_route_ema_blend_state(const void* x, int64_t x_sb, int64_t x_st, const float* logits, const float* b2,
+                               const float* gate, int L, const void* l3, int64_t l3_sb, int64_t l3_st, int T3,
+                               float beta, int B, int T, int D, void* h, int64_t h_sb, int64_t h_st, float* lam,
+                               const float* ema_init, float* ema_final, void* workspace, size_t workspace_bytes,
+                               fmka_stream_t stream) {
+  if (x == nullptr || h == nullptr) return set_error(kErrInvalidArgument, "route_ema_blend_state: null pointer");
+  if (!std::isfinite(beta)) return set_error(kErrInvalidArgument, "route_ema_blend_state: beta must be finite");
+  if (ema_init != nullptr && ema_init == ema_final)
+    return set_error(kErrInvalidArgument, "route_ema_blend_state: ema_init and ema_final must not alias");
+  return launch_route_ema_blend(bf(x), x_sb, x_st, nullptr, 0, 0, logits, b2, gate, L, bf(l3), l3_sb, l3_st, T3,
+                                beta, B, T, D, bfw(h), h_sb, h_st, lam, workspace, workspace_bytes, true,
+                                as_stream(stream), ema_init, ema_final);
+}
 
 int fmka_route_blend(const void* l1, int64_t l1_sb, int64_t l1_st, const void* l2, int64_t l2_sb, int64_t l2_st,
                      const void* l3, int64_t l3_sb, int64_t l3_st, int T3, const float* gate, int L, int B, int T,

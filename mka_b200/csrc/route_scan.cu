@@ -62,6 +62,8 @@ struct ScanParams {
   __nv_bfloat16* h;        // [B, T, D]
   int64_t h_sb, h_st;
   float* lam;              // [B, T, L] or null
+  const float* ema_init;   // [B, D] fp32 EMA state before token 0 (null: zero), scan mode only
+  float* ema_final;        // [B, D] fp32 EMA state after token T-1 (null: not written)
   uint32_t* ticket;
   uint32_t* flags;         // [nseq * nchunks]
   float* agg;              // [nseq * nchunks * kSlice]
@@ -171,6 +173,18 @@ __device__ __forceinline__ void chunk_lookback(const ScanParams& p, int seq, int
     __syncwarp();
     if (lane == 0) st_release_u32(p.flags + rec, kFlagInc);
   }
+}
+
+// b^e for an integer e >= 0 by repeated squaring (exact in sign for b < 0,
+// which exp2(e * log2 b) is not).
+__device__ __forceinline__ float ipow(float b, int e) {
+  float r = 1.f;
+  while (e > 0) {
+    if (e & 1) r *= b;
+    b *= b;
+    e >>= 1;
+  }
+  return r;
 }
 
 __global__ void __launch_bounds__(kThreads, FMKA_SCAN_MINB) route_ema_blend_kernel(const __grid_constant__ ScanParams p) {
@@ -291,6 +305,21 @@ __global__ void __launch_bounds__(kThreads, FMKA_SCAN_MINB) route_ema_blend_kern
       for (int w = 0; w < warp; ++w) v = p.beta8 * v + s_wagg[w][lane * 8 + c];
       st[c] = v;
     }
+    if (p.ema_init != nullptr && ch_ok) {
+      // the scan runs from a zero state; a state s before token 0 adds
+      // beta^t * s to the state entering token t
+      const float dec = ipow(p.beta, tw);
+      const float4 i0 = *reinterpret_cast<const float4*>(p.ema_init + (int64_t)b * p.D + d0);
+      const float4 i1 = *reinterpret_cast<const float4*>(p.ema_init + (int64_t)b * p.D + d0 + 4);
+      st[0] += dec * i0.x;
+      st[1] += dec * i0.y;
+      st[2] += dec * i0.z;
+      st[3] += dec * i0.w;
+      st[4] += dec * i1.x;
+      st[5] += dec * i1.y;
+      st[6] += dec * i1.z;
+      st[7] += dec * i1.w;
+    }
   }
 
   // ---- blend and store ----
@@ -323,6 +352,11 @@ __global__ void __launch_bounds__(kThreads, FMKA_SCAN_MINB) route_ema_blend_kern
       float v = g0 * xf[c] + g1 * st[c];
       if (p.l3 != nullptr) v += g2 * l3f[c];
       o[c] = v;
+    }
+    if (scan && p.ema_final != nullptr && ch_ok && t == p.T - 1) {
+      float* f = p.ema_final + (int64_t)b * p.D + d0;
+      *reinterpret_cast<float4*>(f) = make_float4(st[0], st[1], st[2], st[3]);
+      *reinterpret_cast<float4*>(f + 4) = make_float4(st[4], st[5], st[6], st[7]);
     }
     if (ch_ok && t < p.T) {
       uint4 w;
@@ -357,8 +391,12 @@ int launch_route_ema_blend(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, c
                            const float* b2, const float* gate, int L, const __nv_bfloat16* l3, int64_t l3_sb,
                            int64_t l3_st, int T3, float beta, int B, int T, int D, __nv_bfloat16* h,
                            int64_t h_sb, int64_t h_st, float* lam, void* workspace, size_t workspace_bytes,
-                           bool clear_flags, cudaStream_t stream) {
+                           bool clear_flags, cudaStream_t stream, const float* ema_init, float* ema_final) {
   if (B <= 0 || T <= 0 || D <= 0) return set_error(kErrInvalidArgument, "route_ema_blend: empty shape");
+  if (l2 != nullptr && (ema_init != nullptr || ema_final != nullptr))
+    return set_error(kErrInvalidArgument, "route_ema_blend: an EMA state needs the scan (no given L2)");
+  if ((reinterpret_cast<uintptr_t>(ema_init) | reinterpret_cast<uintptr_t>(ema_final)) & 15u)
+    return set_error(kErrInvalidArgument, "route_ema_blend: EMA states must be 16-byte aligned");
   if (D % 8 != 0) return set_error(kErrUnsupported, "route_ema_blend: d_model must be a multiple of 8");
   if (L < 2 || L > 3) return set_error(kErrInvalidArgument, "route_ema_blend: levels must be 2 or 3");
   if (L == 3 && (l3 == nullptr || T3 < 1))
@@ -403,6 +441,8 @@ int launch_route_ema_blend(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, c
   p.h_sb = h_sb;
   p.h_st = h_st;
   p.lam = lam;
+  p.ema_init = ema_init;
+  p.ema_final = ema_final;
   p.nds = (D + kSlice - 1) / kSlice;
   p.nchunks = (T + kChunkT - 1) / kChunkT;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -480,7 +520,8 @@ int launch_route_ema_blend_static_scratch(const __nv_bfloat16* x, int64_t x_sb, 
     scratch = g_static_scratch_dev[dev];
   }
   return launch_route_ema_blend(x, x_sb, x_st, nullptr, 0, 0, logits, b2, gate, L, l3, l3_sb, l3_st, T3, beta, B, T,
-                                D, h, h_sb, h_st, lam, scratch, kStaticScratchBytes, /*clear_flags=*/true, stream);
+                                D, h, h_sb, h_st, lam, scratch, kStaticScratchBytes, /*clear_flags=*/true, stream,
+                                nullptr, nullptr);
 }
 
 }  // namespace fmka

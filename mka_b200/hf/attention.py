@@ -120,10 +120,15 @@ class HFFastMKAAttention(nn.Module):
             elif isinstance(past_key_value, StaticKVCache):
                 cache = past_key_value
                 kc, vc = cache.layer(self)
+                ema_in = ema_out = None
+                if cache.carry_ema:
+                    ema_in, ema_out = cache.ema_buffers(self, hidden_states.shape[2], hidden_states.device)
                 r = fastmka_forward(hidden_states, W, self.num_heads, self.num_key_value_heads, self.ema_beta,
                                     self.use_l3, l3_memory=l3_memory, rope=rope, kv_out=(kc, vc),
-                                    past_len=cache.length(self))
+                                    past_len=cache.length(self), ema_state=ema_in, ema_out=ema_out)
                 cache.advance(self, hidden_states.shape[1])
+                if cache.carry_ema:
+                    cache.commit_ema(self)
                 present = (r["k"], r["v"]) if use_cache else None
             else:
                 past = None

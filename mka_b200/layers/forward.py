@@ -33,7 +33,8 @@ def fastmka_forward(x: torch.Tensor, W: PreparedWeights, num_heads: int, num_kv_
                     kv_out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
                     past_len: Optional[int] = None, timers: Optional[list] = None,
                     kv_update: Optional[Callable[[torch.Tensor, torch.Tensor],
-                                                 Tuple[torch.Tensor, torch.Tensor]]] = None) -> dict:
+                                                 Tuple[torch.Tensor, torch.Tensor]]] = None,
+                    ema_state: Optional[torch.Tensor] = None, ema_out: Optional[torch.Tensor] = None) -> dict:
     """Runs the layer on x [B, T, D] (any float dtype; computed in bf16).
 
     past:    (k, v) [B, Hkv, Tp, 128] cached keys/values; the returned k/v are
@@ -47,6 +48,9 @@ def fastmka_forward(x: torch.Tensor, W: PreparedWeights, num_heads: int, num_kv_
     kv_update: alternatively a callable given this call's new (k, v)
              [B, Hkv, T, 128] (post-RoPE) that returns the full (k, v) to attend
              to, e.g. a transformers Cache's update(k, v, layer_idx).
+    ema_state / ema_out: fp32 [B, D] EMA state before this call's first token
+             (None: zero, the reference's restart) and a buffer for the state
+             after its last token, to carry the L2 memory across calls.
     Returns dict(out [B,T,D] bf16, k, v, lam [B,T,L] fp32, lse).
     """
     def mark(name):
@@ -89,7 +93,8 @@ def fastmka_forward(x: torch.Tensor, W: PreparedWeights, num_heads: int, num_kv_
             if l3.shape[0] != B or l3.shape[2] != D:
                 raise RuntimeError("l3_memory must be [B, T3, D]")
     mark("route_ema_blend")
-    h, lam = ops.route_ema_blend(xb, beta, logits=logits, b2=W.b2, levels=L, l3=l3)
+    h, lam = ops.route_ema_blend(xb, beta, logits=logits, b2=W.b2, levels=L, l3=l3, ema_state=ema_state,
+                                 ema_out=ema_out)
     done()
     mark("kv_proj")
     # 3. K/V of the fused memory

@@ -190,13 +190,23 @@ def _rope_args(rope, B: int, T: int):
 def route_ema_blend(x: torch.Tensor, beta: float, logits: Optional[torch.Tensor] = None,
                     b2: Optional[torch.Tensor] = None, gate: Optional[torch.Tensor] = None,
                     levels: int = 2, l3: Optional[torch.Tensor] = None,
-                    want_lam: bool = True) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+                    want_lam: bool = True, ema_state: Optional[torch.Tensor] = None,
+                    ema_out: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
     """H = lam0 * x + lam1 * EMA(x) (+ lam2 * L3) with lam = softmax(logits + b2) (or `gate`).
 
     x [B, T, D] bf16 (token rows contiguous in D); l3 [B, T3, D] bf16 or None.
-    Returns H [B, T, D] bf16 and lam [B, T, L] fp32.
+    ema_state: fp32 [B, D] EMA state before token 0 (None: zero, the
+    reference's restart on every call); ema_out: fp32 [B, D] buffer that
+    receives the state after token T-1. Returns H [B, T, D] bf16 and lam
+    [B, T, L] fp32.
     """
-    _check_cuda(x, logits, gate, l3)
+    _check_cuda(x, logits, gate, l3, ema_state, ema_out)
+    for name, t in (("ema_state", ema_state), ("ema_out", ema_out)):
+        if t is not None and (t.dtype != torch.float32 or tuple(t.shape) != (x.shape[0], x.shape[2])
+                              or not t.is_contiguous()):
+            raise RuntimeError(f"route_ema_blend: {name} must be a contiguous fp32 [B, D] tensor")
+    if ema_state is not None and ema_out is not None and ema_state.data_ptr() == ema_out.data_ptr():
+        raise RuntimeError("route_ema_blend: ema_state and ema_out must be different buffers")
     _check_bf16(x, l3)
     B, T, D = x.shape
     if x.stride(2) != 1:
@@ -217,21 +227,30 @@ def route_ema_blend(x: torch.Tensor, beta: float, logits: Optional[torch.Tensor]
     b2c = _f32(b2)
     logits_c = None if logits is None else logits.contiguous()
     gate_c = None if gate is None else gate.to(torch.float32).contiguous()
-    _lib.call("fmka_route_ema_blend", x.data_ptr(), x.stride(0), x.stride(1), _ptr(logits_c), _ptr(b2c),
-              _ptr(gate_c), levels, _ptr(l3), l3_sb, l3_st, T3, float(beta), B, T, D, h.data_ptr(),
-              h.stride(0), h.stride(1), _ptr(lam), _ptr(ws), ws_bytes, _stream(x))
+    if ema_state is None and ema_out is None:
+        _lib.call("fmka_route_ema_blend", x.data_ptr(), x.stride(0), x.stride(1), _ptr(logits_c), _ptr(b2c),
+                  _ptr(gate_c), levels, _ptr(l3), l3_sb, l3_st, T3, float(beta), B, T, D, h.data_ptr(),
+                  h.stride(0), h.stride(1), _ptr(lam), _ptr(ws), ws_bytes, _stream(x))
+    else:
+        _lib.call("fmka_route_ema_blend_state", x.data_ptr(), x.stride(0), x.stride(1), _ptr(logits_c), _ptr(b2c),
+                  _ptr(gate_c), levels, _ptr(l3), l3_sb, l3_st, T3, float(beta), B, T, D, h.data_ptr(),
+                  h.stride(0), h.stride(1), _ptr(lam), _ptr(ema_state), _ptr(ema_out), _ptr(ws), ws_bytes,
+                  _stream(x))
     return h, lam
 
 
-def causal_prefix_ema(x: torch.Tensor, beta: float = 0.9) -> torch.Tensor:
-    """L2[t] = beta * L2[t-1] + (1 - beta) * x[t] with L2[-1] = 0 (session_memory.py:6-22).
+def causal_prefix_ema(x: torch.Tensor, beta: float = 0.9, state: Optional[torch.Tensor] = None,
+                      state_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """L2[t] = beta * L2[t-1] + (1 - beta) * x[t] with L2[-1] = 0 (session_memory.py:6-22),
+    or L2[-1] = `state` (fp32 [B, D]) to continue an earlier call; `state_out`
+    (fp32 [B, D]) receives L2[T-1].
 
     Runs the stage-1 kernel with the gate fixed to (0, 1), so H == EMA(x).
     """
     B, T, _ = x.shape
     gate = torch.zeros((B * T, 2), dtype=torch.float32, device=x.device)
     gate[:, 1] = 1.0
-    h, _ = route_ema_blend(x, beta, gate=gate, levels=2, want_lam=False)
+    h, _ = route_ema_blend(x, beta, gate=gate, levels=2, want_lam=False, ema_state=state, ema_out=state_out)
     return h
 
 

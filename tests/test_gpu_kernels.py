@@ -144,6 +144,39 @@ def test_causal_prefix_ema_op(ops):
     assert _rel(out, _ref_ema(x.float(), 0.9)) < 1e-2
 
 
+@pytest.mark.parametrize("T1,T2,D,beta", [(173, 127, 3584, 0.9), (64, 1, 136, 0.99), (1, 1, 264, 0.5),
+                                         (700, 45, 520, 0.999)])
+def test_ema_carried_state(ops, T1, T2, D, beta):
+    """Two calls with the state carried equal one call over the whole sequence:
+    the EMA of the reference (L2[-1] = 0, session_memory.py:6-22) continued."""
+    g = torch.Generator(device="cuda").manual_seed(T1 * 31 + T2)
+    B = 2
+    x = torch.randn(B, T1 + T2, D, device="cuda", generator=g).bfloat16()
+    s1 = torch.empty(B, D, device="cuda")
+    s2 = torch.empty(B, D, device="cuda")
+    a = ops.causal_prefix_ema(x[:, :T1].contiguous(), beta, state_out=s1)
+    b = ops.causal_prefix_ema(x[:, T1:].contiguous(), beta, state=s1, state_out=s2)
+    whole = ops.causal_prefix_ema(x, beta)
+    ref = _ref_ema(x.float(), beta)
+    assert ops.device_status() == 0
+    assert _rel(a, ref[:, :T1]) < 1e-2
+    assert _rel(b, ref[:, T1:]) < 1e-2
+    assert (b.float() - whole[:, T1:].float()).abs().max().item() <= 2 ** -7 * ref.abs().max().item()
+    # the carried states are fp32: they match the fp32 recurrence closely
+    assert _rel(s1, ref[:, T1 - 1]) < 1e-4
+    assert _rel(s2, ref[:, -1]) < 1e-4
+    # a state on a blend with a gate and a third level goes through the same scan
+    gate = torch.rand(B * T2, 3, device="cuda", generator=g)
+    gate = gate / gate.sum(-1, keepdim=True)
+    l3 = torch.randn(B, 1, D, device="cuda", generator=g).bfloat16()
+    h, _ = ops.route_ema_blend(x[:, T1:].contiguous(), beta, gate=gate, levels=3, l3=l3, ema_state=s1)
+    gv = gate.view(B, T2, 3)
+    want = gv[..., 0:1] * x[:, T1:].float() + gv[..., 1:2] * ref[:, T1:] + gv[..., 2:3] * l3.float()
+    assert _rel(h, want) < 1e-2
+    with pytest.raises(Exception):
+        ops.causal_prefix_ema(x[:, :T1].contiguous(), beta, state=s1, state_out=s1)
+
+
 @pytest.mark.parametrize("B,Hq,Hkv,Tq,Tk,causal", [(1, 1, 1, 128, 128, True), (2, 4, 2, 200, 200, True),
                                                    (1, 7, 1, 300, 300, True), (2, 2, 2, 64, 333, True),
                                                    (1, 2, 1, 130, 257, False), (1, 4, 4, 1024, 1024, True)])

@@ -270,3 +270,42 @@ def _hf_like_layer(seed=0, D=512, H=4, HKV=2, R=256):
                 if m.bias is not None:
                     m.bias.uniform_(-0.1, 0.1)
     return layer.cuda().eval()
+
+
+def test_hf_decode_carried_ema_matches_whole_sequence_prefill():
+    """With StaticKVCache(carry_ema=True) each decode step continues the L2 EMA
+    of the earlier tokens, so the step's output equals the reference forward
+    over the whole sequence so far at its last position (hf/attention.py:82-199
+    with causal_prefix_ema over all tokens)."""
+    from mka_b200 import StaticKVCache
+
+    D, H, HKV = 512, 4, 2
+    layer = _hf_like_layer(seed=3, D=D, H=H, HKV=HKV)
+    f = lambda t: None if t is None else t.detach().float().cpu()  # noqa: E731
+    p = {"wq": f(layer.q_proj.weight), "bq": f(layer.q_proj.bias), "wk": f(layer.k_proj.weight),
+         "bk": f(layer.k_proj.bias), "wv": f(layer.v_proj.weight), "bv": f(layer.v_proj.bias),
+         "wo": f(layer.o_proj.weight), "r1w": f(layer.router[0].weight), "r1b": f(layer.router[0].bias),
+         "r2w": f(layer.router[2].weight), "r2b": f(layer.router[2].bias)}
+    g = torch.Generator().manual_seed(5)
+    T0, steps = 150, 3
+    x = (torch.randn(2, T0 + steps, D, generator=g) * 0.5).bfloat16()
+    cache = StaticKVCache(batch=2, num_kv_heads=HKV, capacity=T0 + steps, num_layers=1, device="cuda",
+                          carry_ema=True)
+    with torch.no_grad():
+        out, _, _ = layer(x[:, :T0].cuda(), past_key_value=cache, use_cache=True)
+        ref = orc.hf_fastmka_forward(x[:, :T0].float(), p, H, HKV, False, layer.ema_beta, "silu")
+        assert nrel(out, ref["out"]) < TOL
+        for i in range(steps):
+            t = T0 + i
+            out, _, _ = layer(x[:, t:t + 1].cuda(), past_key_value=cache, use_cache=True)
+            whole = orc.hf_fastmka_forward(x[:, :t + 1].float(), p, H, HKV, False, layer.ema_beta, "silu")
+            assert nrel(out, whole["out"][:, -1:]) < TOL, i
+    assert cache.lengths[0] == T0 + steps
+    # without the carried state a decode step restarts the EMA, as the reference does
+    cache2 = StaticKVCache(batch=2, num_kv_heads=HKV, capacity=T0 + 1, num_layers=1, device="cuda")
+    with torch.no_grad():
+        layer(x[:, :T0].cuda(), past_key_value=cache2, use_cache=True)
+        out2, _, _ = layer(x[:, T0:T0 + 1].cuda(), past_key_value=cache2, use_cache=True)
+        ref2 = orc.hf_fastmka_forward(x[:, T0:T0 + 1].float(), p, H, HKV, False, layer.ema_beta, "silu",
+                                      past=(ref["k"], ref["v"]))
+    assert nrel(out2, ref2["out"]) < TOL
