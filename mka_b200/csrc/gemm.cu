@@ -15,10 +15,14 @@
 //                 router        bias + SiLU/GELU + dot with the router's second
 //                               layer, accumulated into per-token gate logits
 // The accumulator is double-buffered so the epilogue of tile i overlaps the
-// main loop of tile i+1.
+// main loop of tile i+1. With at least two 128-row blocks and 256-wide tiles,
+// a CTA-pair kernel (2-SM MMA, 256 x 256 tiles, half the B tile per CTA)
+// runs instead; both share the epilogue.
 //
 // Replaces the nn.Linear calls of the reference FastMKA forward
 // (mka/layers/fastmka.py:79,91,98-99,176; mka/hf/attention.py:95,104,110-111,195).
+#include <cstdlib>
+
 #include "fmka_internal.h"
 #include "ptx.cuh"
 
@@ -63,6 +67,171 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const uint32_t (
 #pragma unroll
     for (int j = 0; j < 32; ++j)
       if (j < nvalid) dst[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+  }
+}
+
+// Fused epilogue of one accumulator tile for the calling thread's row `m` (a
+// warp's lanes hold 32 consecutive rows): columns n0 .. n0+BN-1 of the output
+// from TMEM at acc_addr (this warp's lane quarter, the tile's first column).
+template <int BN>
+__device__ __forceinline__ void gemm_epilogue_tile(const GemmParams& p, int m, bool row_ok, int n0,
+                                                   uint32_t acc_addr) {
+  const GemmSeg& sg = (n0 >= p.n_split) ? p.seg[1] : p.seg[0];
+
+  if (sg.kind == kSegRowMajor) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(acc_addr + c * 32, r);
+      tmem_wait_ld();
+      const int n = n0 + c * 32;
+      if (sg.bias != nullptr) {
+        if (n + 32 <= sg.n_end) {
+          const float4* b4 = reinterpret_cast<const float4*>(sg.bias + (n - sg.n_begin));
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 bb = __ldg(b4 + q);
+            r[4 * q + 0] = __float_as_uint(__uint_as_float(r[4 * q + 0]) + bb.x);
+            r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + bb.y);
+            r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + bb.z);
+            r[4 * q + 3] = __float_as_uint(__uint_as_float(r[4 * q + 3]) + bb.w);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n + j < sg.n_end) r[j] = __float_as_uint(__uint_as_float(r[j]) + __ldg(sg.bias + (n + j - sg.n_begin)));
+        }
+      }
+      if (row_ok && n < sg.n_end) {
+        store_row32(sg.out + (int64_t)m * sg.ld + (n - sg.n_begin), r, sg.n_end - n);
+      }
+    }
+  } else if (sg.kind == kSegHeads) {
+    const int b = row_ok ? m / sg.T : 0;
+    const int t = row_ok ? m % sg.T : 0;
+    const bool rope = sg.rope_cos != nullptr;
+    const int64_t rope_off = (int64_t)b * sg.rope_sb + (int64_t)t * sg.rope_st;
+    __nv_bfloat16* dst_row = sg.out + (int64_t)b * sg.s_b + (int64_t)(t + sg.t_offset) * sg.s_t;
+    // 16-column chunks of the first half of every head (dims d) paired with
+    // the same chunk of the second half (dims d + 64); the RoPE table slice
+    // is loaded once per chunk and shared by the tile's heads.
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float cs1[16], sn1[16], cs2[16], sn2[16];
+      if (rope && row_ok) {
+        const float4* c4a = reinterpret_cast<const float4*>(sg.rope_cos + rope_off + c * 16);
+        const float4* s4a = reinterpret_cast<const float4*>(sg.rope_sin + rope_off + c * 16);
+        const float4* c4b = reinterpret_cast<const float4*>(sg.rope_cos + rope_off + 64 + c * 16);
+        const float4* s4b = reinterpret_cast<const float4*>(sg.rope_sin + rope_off + 64 + c * 16);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 a0 = __ldg(c4a + q), a1 = __ldg(s4a + q), a2 = __ldg(c4b + q), a3 = __ldg(s4b + q);
+          cs1[4 * q] = a0.x; cs1[4 * q + 1] = a0.y; cs1[4 * q + 2] = a0.z; cs1[4 * q + 3] = a0.w;
+          sn1[4 * q] = a1.x; sn1[4 * q + 1] = a1.y; sn1[4 * q + 2] = a1.z; sn1[4 * q + 3] = a1.w;
+          cs2[4 * q] = a2.x; cs2[4 * q + 1] = a2.y; cs2[4 * q + 2] = a2.z; cs2[4 * q + 3] = a2.w;
+          sn2[4 * q] = a3.x; sn2[4 * q + 1] = a3.y; sn2[4 * q + 2] = a3.z; sn2[4 * q + 3] = a3.w;
+        }
+      }
+#pragma unroll
+      for (int hh = 0; hh < BN / 128; ++hh) {
+        uint32_t r1[16], r2[16];
+        tmem_ld16(acc_addr + hh * 128 + c * 16, r1);
+        tmem_ld16(acc_addr + hh * 128 + 64 + c * 16, r2);
+        tmem_wait_ld();
+        const int nl_head = n0 - sg.n_begin + hh * 128;
+        const bool in_range = (n0 + hh * 128) < sg.n_end;
+        if (sg.bias != nullptr && in_range) {
+          const float4* ba = reinterpret_cast<const float4*>(sg.bias + nl_head + c * 16);
+          const float4* bb = reinterpret_cast<const float4*>(sg.bias + nl_head + 64 + c * 16);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 x = __ldg(ba + q), y = __ldg(bb + q);
+            r1[4 * q] = __float_as_uint(__uint_as_float(r1[4 * q]) + x.x);
+            r1[4 * q + 1] = __float_as_uint(__uint_as_float(r1[4 * q + 1]) + x.y);
+            r1[4 * q + 2] = __float_as_uint(__uint_as_float(r1[4 * q + 2]) + x.z);
+            r1[4 * q + 3] = __float_as_uint(__uint_as_float(r1[4 * q + 3]) + x.w);
+            r2[4 * q] = __float_as_uint(__uint_as_float(r2[4 * q]) + y.x);
+            r2[4 * q + 1] = __float_as_uint(__uint_as_float(r2[4 * q + 1]) + y.y);
+            r2[4 * q + 2] = __float_as_uint(__uint_as_float(r2[4 * q + 2]) + y.z);
+            r2[4 * q + 3] = __float_as_uint(__uint_as_float(r2[4 * q + 3]) + y.w);
+          }
+        }
+        uint32_t o1[8], o2[8];
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+          float a0 = __uint_as_float(r1[j]), a1 = __uint_as_float(r1[j + 1]);
+          float b0 = __uint_as_float(r2[j]), b1 = __uint_as_float(r2[j + 1]);
+          if (rope) {
+            const float ra0 = a0 * cs1[j] - b0 * sn1[j];
+            const float ra1 = a1 * cs1[j + 1] - b1 * sn1[j + 1];
+            const float rb0 = b0 * cs2[j] + a0 * sn2[j];
+            const float rb1 = b1 * cs2[j + 1] + a1 * sn2[j + 1];
+            a0 = ra0; a1 = ra1; b0 = rb0; b1 = rb1;
+          }
+          o1[j / 2] = pack_bf16x2(a0, a1);
+          o2[j / 2] = pack_bf16x2(b0, b1);
+        }
+        if (row_ok && in_range) {
+          __nv_bfloat16* dst = dst_row + (int64_t)(nl_head / 128) * sg.s_h;
+          uint4* d1 = reinterpret_cast<uint4*>(dst + c * 16);
+          uint4* d2 = reinterpret_cast<uint4*>(dst + 64 + c * 16);
+          d1[0] = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+          d1[1] = make_uint4(o1[4], o1[5], o1[6], o1[7]);
+          d2[0] = make_uint4(o2[0], o2[1], o2[2], o2[3]);
+          d2[1] = make_uint4(o2[4], o2[5], o2[6], o2[7]);
+        }
+      }
+    }
+  } else {  // kSegRouter
+    float part[4] = {0.f, 0.f, 0.f, 0.f};
+    const int R = sg.n_end - sg.n_begin;
+    const int L = sg.L;
+    const int act = sg.act;
+    const float* w2 = sg.w2;
+    const float* bias = sg.bias;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      const int nl = n0 - sg.n_begin + c * 32;
+      uint32_t r[32];
+      tmem_ld32(acc_addr + c * 32, r);
+      tmem_wait_ld();
+      if (nl >= R) continue;  // warp-uniform
+      if (nl + 32 <= R && (R & 3) == 0) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (bias != nullptr) bb = __ldg(reinterpret_cast<const float4*>(bias + nl) + q);
+          const float a0 = act_fn(__uint_as_float(r[4 * q + 0]) + bb.x, act);
+          const float a1 = act_fn(__uint_as_float(r[4 * q + 1]) + bb.y, act);
+          const float a2 = act_fn(__uint_as_float(r[4 * q + 2]) + bb.z, act);
+          const float a3 = act_fn(__uint_as_float(r[4 * q + 3]) + bb.w, act);
+#pragma unroll
+          for (int l = 0; l < 4; ++l) {
+            if (l < L) {
+              const float4 w = __ldg(reinterpret_cast<const float4*>(w2 + (int64_t)l * R + nl) + q);
+              part[l] += w.x * a0 + w.y * a1 + w.z * a2 + w.w * a3;
+            }
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (nl + j < R) {
+            float v = __uint_as_float(r[j]);
+            if (bias != nullptr) v += __ldg(bias + nl + j);
+            const float a = act_fn(v, act);
+#pragma unroll
+            for (int l = 0; l < 4; ++l)
+              if (l < L) part[l] += __ldg(w2 + (int64_t)l * R + nl + j) * a;
+          }
+        }
+      }
+    }
+    if (row_ok) {
+#pragma unroll
+      for (int l = 0; l < 4; ++l)
+        if (l < L) atomicAdd(sg.logits + (int64_t)m * L + l, part[l]);
+    }
   }
 }
 
@@ -223,164 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n0 = (tile % num_n) * BN;
       const int m = m0 + row_in_tile;
       const bool row_ok = m < p.M;
-      const GemmSeg& sg = (n0 >= p.n_split) ? p.seg[1] : p.seg[0];
-      const uint32_t acc_addr = lane_addr + acc * BN;
-
-      if (sg.kind == kSegRowMajor) {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(acc_addr + c * 32, r);
-          tmem_wait_ld();
-          const int n = n0 + c * 32;
-          if (sg.bias != nullptr) {
-            if (n + 32 <= sg.n_end) {
-              const float4* b4 = reinterpret_cast<const float4*>(sg.bias + (n - sg.n_begin));
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                const float4 bb = __ldg(b4 + q);
-                r[4 * q + 0] = __float_as_uint(__uint_as_float(r[4 * q + 0]) + bb.x);
-                r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + bb.y);
-                r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + bb.z);
-                r[4 * q + 3] = __float_as_uint(__uint_as_float(r[4 * q + 3]) + bb.w);
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (n + j < sg.n_end) r[j] = __float_as_uint(__uint_as_float(r[j]) + __ldg(sg.bias + (n + j - sg.n_begin)));
-            }
-          }
-          if (row_ok && n < sg.n_end) {
-            store_row32(sg.out + (int64_t)m * sg.ld + (n - sg.n_begin), r, sg.n_end - n);
-          }
-        }
-      } else if (sg.kind == kSegHeads) {
-        const int b = row_ok ? m / sg.T : 0;
-        const int t = row_ok ? m % sg.T : 0;
-        const bool rope = sg.rope_cos != nullptr;
-        const int64_t rope_off = (int64_t)b * sg.rope_sb + (int64_t)t * sg.rope_st;
-        __nv_bfloat16* dst_row = sg.out + (int64_t)b * sg.s_b + (int64_t)(t + sg.t_offset) * sg.s_t;
-        // 16-column chunks of the first half of every head (dims d) paired with
-        // the same chunk of the second half (dims d + 64); the RoPE table slice
-        // is loaded once per chunk and shared by the tile's heads.
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float cs1[16], sn1[16], cs2[16], sn2[16];
-          if (rope && row_ok) {
-            const float4* c4a = reinterpret_cast<const float4*>(sg.rope_cos + rope_off + c * 16);
-            const float4* s4a = reinterpret_cast<const float4*>(sg.rope_sin + rope_off + c * 16);
-            const float4* c4b = reinterpret_cast<const float4*>(sg.rope_cos + rope_off + 64 + c * 16);
-            const float4* s4b = reinterpret_cast<const float4*>(sg.rope_sin + rope_off + 64 + c * 16);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const float4 a0 = __ldg(c4a + q), a1 = __ldg(s4a + q), a2 = __ldg(c4b + q), a3 = __ldg(s4b + q);
-              cs1[4 * q] = a0.x; cs1[4 * q + 1] = a0.y; cs1[4 * q + 2] = a0.z; cs1[4 * q + 3] = a0.w;
-              sn1[4 * q] = a1.x; sn1[4 * q + 1] = a1.y; sn1[4 * q + 2] = a1.z; sn1[4 * q + 3] = a1.w;
-              cs2[4 * q] = a2.x; cs2[4 * q + 1] = a2.y; cs2[4 * q + 2] = a2.z; cs2[4 * q + 3] = a2.w;
-              sn2[4 * q] = a3.x; sn2[4 * q + 1] = a3.y; sn2[4 * q + 2] = a3.z; sn2[4 * q + 3] = a3.w;
-            }
-          }
-#pragma unroll
-          for (int hh = 0; hh < BN / 128; ++hh) {
-            uint32_t r1[16], r2[16];
-            tmem_ld16(acc_addr + hh * 128 + c * 16, r1);
-            tmem_ld16(acc_addr + hh * 128 + 64 + c * 16, r2);
-            tmem_wait_ld();
-            const int nl_head = n0 - sg.n_begin + hh * 128;
-            const bool in_range = (n0 + hh * 128) < sg.n_end;
-            if (sg.bias != nullptr && in_range) {
-              const float4* ba = reinterpret_cast<const float4*>(sg.bias + nl_head + c * 16);
-              const float4* bb = reinterpret_cast<const float4*>(sg.bias + nl_head + 64 + c * 16);
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const float4 x = __ldg(ba + q), y = __ldg(bb + q);
-                r1[4 * q] = __float_as_uint(__uint_as_float(r1[4 * q]) + x.x);
-                r1[4 * q + 1] = __float_as_uint(__uint_as_float(r1[4 * q + 1]) + x.y);
-                r1[4 * q + 2] = __float_as_uint(__uint_as_float(r1[4 * q + 2]) + x.z);
-                r1[4 * q + 3] = __float_as_uint(__uint_as_float(r1[4 * q + 3]) + x.w);
-                r2[4 * q] = __float_as_uint(__uint_as_float(r2[4 * q]) + y.x);
-                r2[4 * q + 1] = __float_as_uint(__uint_as_float(r2[4 * q + 1]) + y.y);
-                r2[4 * q + 2] = __float_as_uint(__uint_as_float(r2[4 * q + 2]) + y.z);
-                r2[4 * q + 3] = __float_as_uint(__uint_as_float(r2[4 * q + 3]) + y.w);
-              }
-            }
-            uint32_t o1[8], o2[8];
-#pragma unroll
-            for (int j = 0; j < 16; j += 2) {
-              float a0 = __uint_as_float(r1[j]), a1 = __uint_as_float(r1[j + 1]);
-              float b0 = __uint_as_float(r2[j]), b1 = __uint_as_float(r2[j + 1]);
-              if (rope) {
-                const float ra0 = a0 * cs1[j] - b0 * sn1[j];
-                const float ra1 = a1 * cs1[j + 1] - b1 * sn1[j + 1];
-                const float rb0 = b0 * cs2[j] + a0 * sn2[j];
-                const float rb1 = b1 * cs2[j + 1] + a1 * sn2[j + 1];
-                a0 = ra0; a1 = ra1; b0 = rb0; b1 = rb1;
-              }
-              o1[j / 2] = pack_bf16x2(a0, a1);
-              o2[j / 2] = pack_bf16x2(b0, b1);
-            }
-            if (row_ok && in_range) {
-              __nv_bfloat16* dst = dst_row + (int64_t)(nl_head / 128) * sg.s_h;
-              uint4* d1 = reinterpret_cast<uint4*>(dst + c * 16);
-              uint4* d2 = reinterpret_cast<uint4*>(dst + 64 + c * 16);
-              d1[0] = make_uint4(o1[0], o1[1], o1[2], o1[3]);
-              d1[1] = make_uint4(o1[4], o1[5], o1[6], o1[7]);
-              d2[0] = make_uint4(o2[0], o2[1], o2[2], o2[3]);
-              d2[1] = make_uint4(o2[4], o2[5], o2[6], o2[7]);
-            }
-          }
-        }
-      } else {  // kSegRouter
-        float part[4] = {0.f, 0.f, 0.f, 0.f};
-        const int R = sg.n_end - sg.n_begin;
-        const int L = sg.L;
-        const int act = sg.act;
-        const float* w2 = sg.w2;
-        const float* bias = sg.bias;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          const int nl = n0 - sg.n_begin + c * 32;
-          uint32_t r[32];
-          tmem_ld32(acc_addr + c * 32, r);
-          tmem_wait_ld();
-          if (nl >= R) continue;  // warp-uniform
-          if (nl + 32 <= R && (R & 3) == 0) {
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
-              if (bias != nullptr) bb = __ldg(reinterpret_cast<const float4*>(bias + nl) + q);
-              const float a0 = act_fn(__uint_as_float(r[4 * q + 0]) + bb.x, act);
-              const float a1 = act_fn(__uint_as_float(r[4 * q + 1]) + bb.y, act);
-              const float a2 = act_fn(__uint_as_float(r[4 * q + 2]) + bb.z, act);
-              const float a3 = act_fn(__uint_as_float(r[4 * q + 3]) + bb.w, act);
-#pragma unroll
-              for (int l = 0; l < 4; ++l) {
-                if (l < L) {
-                  const float4 w = __ldg(reinterpret_cast<const float4*>(w2 + (int64_t)l * R + nl) + q);
-                  part[l] += w.x * a0 + w.y * a1 + w.z * a2 + w.w * a3;
-                }
-              }
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (nl + j < R) {
-                float v = __uint_as_float(r[j]);
-                if (bias != nullptr) v += __ldg(bias + nl + j);
-                const float a = act_fn(v, act);
-#pragma unroll
-                for (int l = 0; l < 4; ++l)
-                  if (l < L) part[l] += __ldg(w2 + (int64_t)l * R + nl + j) * a;
-              }
-            }
-          }
-        }
-        if (row_ok) {
-#pragma unroll
-          for (int l = 0; l < 4; ++l)
-            if (l < L) atomicAdd(sg.logits + (int64_t)m * L + l, part[l]);
-        }
-      }
+      gemm_epilogue_tile<BN>(p, m, row_ok, n0, lane_addr + acc * BN);
       tc_fence_before();
       __syncwarp();  // every lane's TMEM reads have completed before the warp's arrival
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -393,6 +405,205 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant: a cluster of two CTAs on neighbouring SMs computes
+// 256 x 256 tiles with the 2-SM MMA (M = 256, cta_group::2), issued by the
+// even CTA. Each CTA loads only its own 128 A rows and its half (128 rows) of
+// the B tile, so a stage is 32 KB per CTA instead of 48 KB: a third less
+// operand traffic per FLOP and six stages of loads in flight. Each CTA's TMEM
+// holds its 128 rows x 256 columns of the accumulator (double-buffered), and
+// each CTA runs the same epilogue on its rows.
+// Synchronisation: both CTAs' TMA loads complete on the even CTA's `full`
+// barrier (the even CTA's producer posts the byte count of both); the MMA's
+// commits arrive on `empty` / `tfull` in both CTAs; both CTAs' epilogue warps
+// arrive on the even CTA's `tempty` (8 arrivals).
+struct PairCfg {
+  static constexpr int kBN = 256;
+  static constexpr int kHalfN = 128;
+  static constexpr int kStages = 6;
+  static constexpr int kABytes = kBM * kBK * 2;     // 16 KB
+  static constexpr int kBBytes = kHalfN * kBK * 2;  // 16 KB
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * kBN;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+};
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ GemmParams p) {
+  using Cfg = PairCfg;
+  constexpr int S = Cfg::kStages;
+  constexpr int BN = Cfg::kBN;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * Cfg::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* full = bars;               // [S]  used in the even CTA
+  uint64_t* empty = bars + S;          // [S]  both CTAs
+  uint64_t* tfull = bars + 2 * S;      // [2]  both CTAs
+  uint64_t* tempty = bars + 2 * S + 2; // [2]  used in the even CTA
+  uint64_t* mma_done = bars + 2 * S + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+
+  const int num_m = (p.M + 2 * kBM - 1) / (2 * kBM);
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (p.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);  // one arrival per epilogue warp of both CTAs
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers are initialised and their TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer --
+    if (lane == 0) {
+      const uint32_t full_even = cluster_addr(&full[0], 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      long issued = 0;
+      for (int tile = pair; tile < num_tiles && !*abort_flag; tile += npairs) {
+        const int m0 = (tile / num_n) * (2 * kBM) + (int)rank * kBM;
+        const int n0 = (tile % num_n) * BN + (int)rank * Cfg::kHalfN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
+            *abort_flag = 1;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
+          const uint32_t fb = full_even + stage * 8;
+          if (p.a_kblk > 0)
+            tma_load_3d_pair(sA + stage * Cfg::kABytes, &tmA, fb, (kb * kBK) % p.a_kblk, m0, (kb * kBK) / p.a_kblk);
+          else
+            tma_load_2d_pair(sA + stage * Cfg::kABytes, &tmA, fb, kb * kBK, m0);
+          tma_load_2d_pair(sB + stage * Cfg::kBBytes, &tmB, fb, kb * kBK, n0);
+          ++issued;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain: the last fills of each stage have been consumed (their MMAs
+      // completed, so their loads landed) before the CTA tears down.
+      const long pending = issued < S ? issued : S;
+      for (long i = 0; i < pending; ++i) {
+        if (--stage < 0) {
+          stage = S - 1;
+          phase ^= 1u;
+        }
+        mbar_wait(&empty[stage], phase, p.status);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------- MMA (the even CTA issues) --
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(2 * kBM, BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int tile = pair; tile < num_tiles && !*abort_flag; tile += npairs, ++it) {
+        const int acc = it & 1;
+        const uint32_t aphase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], aphase ^ 1u, p.status)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * Cfg::kABytes);
+          const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            umma_ss_pair(d_tmem, desc_kmajor_sw128(a_addr + k * 32), desc_kmajor_sw128(b_addr + k * 32), idesc,
+                         (kb | k) != 0);
+          }
+          tc_commit_pair(&empty[stage], 0x3);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_commit_pair(&tfull[acc], 0x3);
+      }
+      // All MMAs (and the commits before this one) complete before teardown.
+      tc_commit_pair(mma_done, 0x1);
+      mbar_wait(mma_done, 0, p.status);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue --
+    const int ew = warp - 4;
+    const int row_in_tile = ew * 32 + lane;
+    const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(ew * 32) << 16);
+    const uint32_t tempty_even = cluster_addr(&tempty[0], 0);
+    int it = 0;
+    for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {
+      const int acc = it & 1;
+      const uint32_t aphase = (it >> 1) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aphase, p.status))) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int m = (tile / num_n) * (2 * kBM) + (int)rank * kBM + row_in_tile;
+      const int n0 = (tile % num_n) * BN;
+      gemm_epilogue_tile<BN>(p, m, m < p.M, n0, lane_addr + acc * BN);
+      tc_fence_before();
+      __syncwarp();  // every lane's TMEM reads have completed before the warp's arrival
+      if (lane == 0) mbar_arrive_cluster(tempty_even + acc * 8);
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // no arrival or commit aimed at either CTA is still outstanding
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
   }
 }
 
@@ -440,12 +651,30 @@ int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int
     int rc = make_tmap_bf16(&tmA, A, 2, dims, strides, box, true);
     if (rc) return rc;
   }
+  // CTA pairs for 256-wide tiles whenever there are at least two 128-row
+  // blocks; FMKA_GEMM_PAIR=0 in the environment selects the one-CTA kernel.
+  static const bool pair_enabled = [] {
+    const char* e = std::getenv("FMKA_GEMM_PAIR");
+    return e == nullptr || e[0] != '0';
+  }();
+  const bool use_pair = pair_enabled && BN == 256 && p.M > kBM && num_sms >= 2;
   {
     uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.N};
     uint64_t strides[1] = {(uint64_t)ldb * 2};
-    uint32_t box[2] = {kBK, (uint32_t)BN};
+    uint32_t box[2] = {kBK, use_pair ? (uint32_t)PairCfg::kHalfN : (uint32_t)BN};
     int rc = make_tmap_bf16(&tmB, B, 2, dims, strides, box, true);
     if (rc) return rc;
+  }
+
+  if (use_pair) {
+    const int tiles = ((p.M + 2 * kBM - 1) / (2 * kBM)) * ((p.N + PairCfg::kBN - 1) / PairCfg::kBN);
+    const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
+    const int smem = PairCfg::kSmemBytes;
+    int rc = check_cuda(cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                        "gemm pair attr");
+    if (rc) return rc;
+    gemm_pair_kernel<<<2 * pairs, kThreads, smem, stream>>>(tmA, tmB, p);
+    return check_cuda(cudaGetLastError(), "gemm pair launch");
   }
 
   const int num_tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN);

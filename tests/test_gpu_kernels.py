@@ -41,7 +41,8 @@ def _ref_attn(q, k, v, causal=True, scale=None):
     return o, lse
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 384, 256), (1000, 1024, 1024), (77, 136, 3584)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 384, 256), (1000, 1024, 1024), (77, 136, 3584),
+                                   (4096, 2048, 512), (2500, 768, 1536), (40000, 512, 128)])
 def test_gemm_plain(ops, M, N, K):
     g = torch.Generator(device="cuda").manual_seed(M + N + K)
     a = torch.randn(M, K, device="cuda", generator=g).bfloat16()
