@@ -620,6 +620,9 @@ int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int
   // Tile width: 256 when every segment boundary is 256-aligned, else 128.
   int BN = 256;
   if (p.n_split % 256 != 0 && p.n_split < p.N) BN = 128;
+  // One row block (decode-sized M): the GEMM streams weights, and narrower
+  // tiles double the number of CTAs pulling them.
+  if (p.M <= kBM) BN = 128;
   if (p.n_split % 128 != 0 && p.n_split < p.N)
     return set_error(kErrInvalidArgument, "gemm: segment split must be a multiple of 128 columns");
   for (int s = 0; s < 2; ++s) {
