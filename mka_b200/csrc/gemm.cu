@@ -607,6 +607,216 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Split-K on a cluster, for GEMMs whose M fits one 64-row slice (decode).
+// Such a GEMM streams the weights; with one CTA per 128-column tile only
+// N/128 CTAs pull them. Here a cluster of S (= kSplitMax) CTAs shares each tile: CTA r
+// runs the main loop over the r-th slice of K into its own TMEM. After a
+// cluster barrier (every main loop and load has finished, so the stage
+// buffers are free), CTAs 1..S-1 store their fp32 partial rows into the stage
+// buffers of CTA 0 through distributed shared memory; after a second barrier
+// CTA 0 adds them to its accumulator in TMEM and runs the fused epilogue once.
+// Every warp of every CTA passes both barriers exactly once, on every path.
+constexpr int kSplitRows = 64;   // rows of a partial that are exchanged
+// Cluster size. Up to 7 partials of 64 x 128 fp32 would fit the 192 KB of
+// stages, but measured on the decode projections (M = 64, K = 4096) pairs are
+// fastest: 2 CTAs per tile beat 1 by 9-18 %, while 4 and 7 lose to 2 (each
+// CTA's pipeline-fill latency and the two cluster barriers outweigh the
+// extra streaming CTAs, and clusters of 7 pack poorly into the GPCs).
+constexpr int kSplitMax = 2;
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const __grid_constant__ GemmParams p) {
+  constexpr int BN = 128;
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  constexpr int kSlotBytes = kSplitRows * BN * 4;  // 32 KB
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * Cfg::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tfull = bars + 2 * S;
+  uint64_t* mma_done = bars + 2 * S + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  uint32_t csize;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(csize));
+  const int tile = blockIdx.x / (int)csize;  // 128-column tile of this cluster
+  const int n0 = tile * BN;
+  const int num_kb = (p.K + kBK - 1) / kBK;
+  // balanced slices: none is empty while the cluster has at most num_kb CTAs
+  const int kb0 = (int)(((long)rank * num_kb) / (int)csize);
+  const int kb1 = (int)(((long)(rank + 1) * num_kb) / (int)csize);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  bool have_acc = false;  // epilogue warps: this CTA's partial is complete in TMEM
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer --
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long issued = 0;
+      for (int kb = kb0; kb < kb1 && !*abort_flag; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+        if (p.a_kblk > 0)
+          tma_load_3d(sA + stage * Cfg::kABytes, &tmA, &full[stage], (kb * kBK) % p.a_kblk, 0, (kb * kBK) / p.a_kblk);
+        else
+          tma_load_2d(sA + stage * Cfg::kABytes, &tmA, &full[stage], kb * kBK, 0);
+        tma_load_2d(sB + stage * Cfg::kBBytes, &tmB, &full[stage], kb * kBK, n0);
+        ++issued;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      const long pending = issued < S ? issued : S;
+      for (long i = 0; i < pending; ++i) {
+        if (--stage < 0) {
+          stage = S - 1;
+          phase ^= 1u;
+        }
+        mbar_wait(&full[stage], phase, p.status);
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA --
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full[stage], phase, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(sA + stage * Cfg::kABytes);
+        const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k) {
+          umma_ss(tmem_base, desc_kmajor_sw128(a_addr + k * 32), desc_kmajor_sw128(b_addr + k * 32), idesc,
+                  (kb > kb0 || k > 0) ? 1u : 0u);
+        }
+        tc_commit(&empty[stage]);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) *abort_flag = 1;
+      tc_commit(tfull);  // also when no MMA ran: the epilogue then sees an error
+      tc_commit(mma_done);
+      mbar_wait(mma_done, 0, p.status);
+    }
+  } else if (warp >= 4) {
+    const bool done = mbar_wait(tfull, 0, p.status);
+    have_acc = __all_sync(0xffffffffu, done && !*abort_flag);
+    if (have_acc) tc_fence_after();
+  }
+
+  // ---- every main loop and TMA load of the cluster is done ----
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const int ew = warp - 4;
+  const int row = ew * 32 + lane;
+  const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(ew * 32) << 16);
+  if (warp >= 4 && rank != 0 && have_acc && ew < kSplitRows / 32) {
+    // partial rows 0..63 into slot rank-1 of CTA 0's stage buffers
+    const uint32_t dst = cluster_addr(smem, 0) + (rank - 1) * kSlotBytes + row * BN * 4;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(lane_addr + c * 32, r);
+      tmem_wait_ld();
+      if (row < p.M) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst + (c * 32 + q * 4) * 4),
+                       "r"(r[4 * q]), "r"(r[4 * q + 1]), "r"(r[4 * q + 2]), "r"(r[4 * q + 3])
+                       : "memory");
+      }
+    }
+  }
+  __syncwarp();
+  cluster_sync();  // the partials have landed in CTA 0
+  if (warp >= 4 && rank == 0) {
+    const bool ok = have_acc;
+    if (ok && ew < kSplitRows / 32) {  // warp-uniform: tcgen05.ld/st are warp-collective
+      const float* slots = reinterpret_cast<const float*>(smem) + row * BN;
+      const int nslots = row < p.M ? (int)csize - 1 : 0;  // per lane: rows past M were never sent
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(lane_addr + c * 32, r);
+        tmem_wait_ld();
+        for (int sl = 0; sl < nslots; ++sl) {
+          const float4* src = reinterpret_cast<const float4*>(slots + sl * (kSlotBytes / 4) + c * 32);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 v = src[q];
+            r[4 * q] = __float_as_uint(__uint_as_float(r[4 * q]) + v.x);
+            r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + v.y);
+            r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + v.z);
+            r[4 * q + 3] = __float_as_uint(__uint_as_float(r[4 * q + 3]) + v.w);
+          }
+        }
+        tmem_st32(lane_addr + c * 32, r);
+      }
+    }
+    tmem_wait_st();
+    if (__all_sync(0xffffffffu, ok)) {
+      gemm_epilogue_tile<BN>(p, row, row < p.M, n0, lane_addr);
+    } else {
+      *abort_flag = 1;
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, BN);
+  }
+}
+
 }  // namespace
 
 int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int64_t ldb, const GemmParams& p,
@@ -667,6 +877,42 @@ int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int
     uint32_t box[2] = {kBK, use_pair ? (uint32_t)PairCfg::kHalfN : (uint32_t)BN};
     int rc = make_tmap_bf16(&tmB, B, 2, dims, strides, box, true);
     if (rc) return rc;
+  }
+
+  // Decode-sized M: split K over a cluster of CTAs per 128-column tile;
+  // FMKA_GEMM_SPLITK=0 in the environment keeps one CTA per tile.
+  static const bool splitk_enabled = [] {
+    const char* e = std::getenv("FMKA_GEMM_SPLITK");
+    return e == nullptr || e[0] != '0';
+  }();
+  if (splitk_enabled && BN == 128 && p.M <= kSplitRows) {
+    const int tiles = (p.N + BN - 1) / BN;
+    const int num_kb = (p.K + kBK - 1) / kBK;
+    int cs = num_sms / tiles;
+    if (cs > kSplitMax) cs = kSplitMax;
+    if (cs > num_kb) cs = num_kb;
+    if (cs >= 2) {
+      const int smem = GemmCfg<128>::kSmemBytes;
+      int rc = check_cuda(
+          cudaFuncSetAttribute(gemm_splitk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+          "gemm split-K attr");
+      if (rc) return rc;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)(tiles * cs), 1, 1);
+      cfg.blockDim = dim3(kThreads, 1, 1);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = (unsigned)cs;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      rc = check_cuda(cudaLaunchKernelEx(&cfg, gemm_splitk_kernel, tmA, tmB, p), "gemm split-K launch");
+      if (rc) return rc;
+      return check_cuda(cudaGetLastError(), "gemm split-K launch");
+    }
   }
 
   if (use_pair) {

@@ -42,7 +42,8 @@ def _ref_attn(q, k, v, causal=True, scale=None):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 384, 256), (1000, 1024, 1024), (77, 136, 3584),
-                                   (4096, 2048, 512), (2500, 768, 1536), (40000, 512, 128)])
+                                   (4096, 2048, 512), (2500, 768, 1536), (40000, 512, 128),
+                                   (64, 6144, 4096), (1, 256, 4096), (50, 384, 576), (33, 1000, 128)])
 def test_gemm_plain(ops, M, N, K):
     g = torch.Generator(device="cuda").manual_seed(M + N + K)
     a = torch.randn(M, K, device="cuda", generator=g).bfloat16()
@@ -54,7 +55,8 @@ def test_gemm_plain(ops, M, N, K):
 
 
 @pytest.mark.parametrize("B,T,Hq,R,rope,act", [(2, 100, 2, 64, False, 1), (1, 256, 4, 512, True, 0),
-                                                (3, 33, 2, 96, True, 1)])
+                                                (3, 33, 2, 96, True, 1), (16, 1, 4, 256, True, 0),
+                                                (60, 1, 2, 128, True, 1)])
 def test_qr_proj(ops, B, T, Hq, R, rope, act):
     D = 256
     L = 3
@@ -207,7 +209,8 @@ def test_attn_decode(ops, B, Hq, Hkv, Tk, splits):
     assert (lse - rlse[..., 0]).abs().max().item() < 2e-2
 
 
-@pytest.mark.parametrize("nblk,M,kb,N", [(2, 300, 896, 384), (4, 1024, 128, 512), (1, 77, 256, 256)])
+@pytest.mark.parametrize("nblk,M,kb,N", [(2, 300, 896, 384), (4, 1024, 128, 512), (1, 77, 256, 256),
+                                         (3, 40, 256, 384)])
 def test_gemm_kblocked(ops, nblk, M, kb, N):
     """A given as blocks of columns (the all-gathered attention output of a head-sharded layer)."""
     g = torch.Generator(device="cuda").manual_seed(nblk * M)
