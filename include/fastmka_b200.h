@@ -23,7 +23,10 @@
  *                            mka/layers/fastmka.py:82-96; mka/hf/attention.py:97-107)
  *   fmka_route_ema_blend_state  the same with the EMA state carried across calls
  *                           (extends session_memory.py:6-22, which restarts at zero)
- *   fmka_kv_proj           k/v projection of the fused memory (+ RoPE on k)
+ *   fmka_route_ema_blend_kv the same for two levels on x [Wk ; Wv]^T, writing K/V
+ *                           (the blend and k/v_proj of fastmka.py:94-99 and
+ *                            hf/attention.py:105-119 in the commuted order)
+ *   fmka_kv_proj            k/v projection of the fused memory (+ RoPE on k)
  *                           (mka/layers/fastmka.py:98-99; mka/hf/attention.py:110-119)
  *   fmka_attn_fwd_prefill   causal attention: fastmka_attn (mka/cuda/ops.py:73,
  *                           mka/cuda/fastmka_attn.cpp:11-17, fastmka_attn.cu:133-172)
@@ -167,6 +170,28 @@ FMKA_API int fmka_route_ema_blend_state(const void* x, int64_t x_sb, int64_t x_s
                                         int64_t h_sb, int64_t h_st, float* lam, const float* ema_init,
                                         float* ema_final, void* workspace, size_t workspace_bytes,
                                         fmka_stream_t stream);
+
+/* fmka_route_ema_blend_kv: stage 1 on the projected memory, for two levels.
+ * Input y = x [Wk ; Wv]^T (bf16 [B, T, 2*Hkv*128], rows y_st apart, batches
+ * y_sb; from fmka_gemm_bf16 without bias). Output the reference's k_proj /
+ * v_proj of the fused memory (mka/hf/attention.py:97-119,
+ * mka/layers/fastmka.py:82-99) head-split into k_out / v_out
+ * ([B, Hkv, Tcap, 128], strides kv_sb, kv_sh, kv_st, written at token slot
+ * t + t_offset): with lam = softmax(logits + b2),
+ *   K = lam0 * yk + lam1 * EMA(yk) + bk, then rotate-half RoPE (cos/sin fp32
+ *   [*, T, 128], may be NULL), and V likewise without RoPE,
+ * which equals projecting lam0 * x + lam1 * EMA(x) because the EMA (along
+ * tokens) commutes with the projection (along channels) and the gate sums to
+ * one. The scan runs over 2*Hkv*128 channels instead of d_model. lam (fp32
+ * [B, T, 2]), ema_init / ema_final (fp32 [B, 2*Hkv*128], the state of
+ * EMA(y), as for fmka_route_ema_blend_state) may be NULL. */
+FMKA_API size_t fmka_route_ema_blend_kv_workspace_size(int B, int T, int Hkv);
+FMKA_API int fmka_route_ema_blend_kv(const void* y, int64_t y_sb, int64_t y_st, const float* logits,
+                                     const float* b2, float beta, int B, int T, int Hkv, const float* bias,
+                                     void* k_out, void* v_out, int64_t kv_sb, int64_t kv_sh, int64_t kv_st,
+                                     int t_offset, const float* rope_cos, const float* rope_sin, int64_t rope_sb,
+                                     int64_t rope_st, float* lam, const float* ema_init, float* ema_final,
+                                     void* workspace, size_t workspace_bytes, fmka_stream_t stream);
 
 /* Route blend with all three memories given (no scan):
  * H = gate0*l1 + gate1*l2 (+ gate2*l3), gate fp32 [B*T, L]. This is the blend

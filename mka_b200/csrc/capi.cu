@@ -23,7 +23,13 @@ int launch_route_ema_blend(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, c
                            int64_t l3_st, int T3, float beta, int B, int T, int D, __nv_bfloat16* h,
                            int64_t h_sb, int64_t h_st, float* lam, void* workspace, size_t workspace_bytes,
                            bool clear_flags, cudaStream_t stream, const float* ema_init = nullptr,
-                           float* ema_final = nullptr);
+                           float* ema_final = nullptr, const struct KvOut* kv = nullptr);
+int launch_route_ema_blend_kv(const __nv_bfloat16* y, int64_t y_sb, int64_t y_st, const float* logits, const float* b2,
+                              float beta, int B, int T, int Hkv, const float* bias, __nv_bfloat16* k_out,
+                              __nv_bfloat16* v_out, int64_t kv_sb, int64_t kv_sh, int64_t kv_st, int t_offset,
+                              const float* rope_cos, const float* rope_sin, int64_t rope_sb, int64_t rope_st,
+                              float* lam, const float* ema_init, float* ema_final, void* workspace,
+                              size_t workspace_bytes, cudaStream_t stream);
 size_t route_ema_blend_static_scratch_bytes();
 int launch_route_ema_blend_static_scratch(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, const float* logits,
                                           const float* b2, const float* gate, int L, const __nv_bfloat16* l3,
@@ -370,6 +376,26 @@ int fmka_route_ema_blend_state(const void* x, int64_t x_sb, int64_t x_st, const 
   return launch_route_ema_blend(bf(x), x_sb, x_st, nullptr, 0, 0, logits, b2, gate, L, bf(l3), l3_sb, l3_st, T3,
                                 beta, B, T, D, bfw(h), h_sb, h_st, lam, workspace, workspace_bytes, true,
                                 as_stream(stream), ema_init, ema_final);
+}
+
+size_t fmka_route_ema_blend_kv_workspace_size(int B, int T, int Hkv) {
+  if (B <= 0 || T <= 0 || Hkv <= 0) return 0;
+  return route_ema_blend_workspace_bytes(B, T, 2 * Hkv * 128);
+}
+
+int fmka_route_ema_blend_kv(const void* y, int64_t y_sb, int64_t y_st, const float* logits, const float* b2,
+                            float beta, int B, int T, int Hkv, const float* bias, void* k_out, void* v_out,
+                            int64_t kv_sb, int64_t kv_sh, int64_t kv_st, int t_offset, const float* rope_cos,
+                            const float* rope_sin, int64_t rope_sb, int64_t rope_st, float* lam,
+                            const float* ema_init, float* ema_final, void* workspace, size_t workspace_bytes,
+                            fmka_stream_t stream) {
+  if (y == nullptr) return set_error(kErrInvalidArgument, "route_ema_blend_kv: null pointer");
+  if (!std::isfinite(beta)) return set_error(kErrInvalidArgument, "route_ema_blend_kv: beta must be finite");
+  if (ema_init != nullptr && ema_init == ema_final)
+    return set_error(kErrInvalidArgument, "route_ema_blend_kv: ema_init and ema_final must not alias");
+  return launch_route_ema_blend_kv(bf(y), y_sb, y_st, logits, b2, beta, B, T, Hkv, bias, bfw(k_out), bfw(v_out),
+                                   kv_sb, kv_sh, kv_st, t_offset, rope_cos, rope_sin, rope_sb, rope_st, lam,
+                                   ema_init, ema_final, workspace, workspace_bytes, as_stream(stream));
 }
 
 int fmka_route_blend(const void* l1, int64_t l1_sb, int64_t l1_st, const void* l2, int64_t l2_sb, int64_t l2_st,

@@ -62,6 +62,18 @@ struct ScanParams {
   __nv_bfloat16* h;        // [B, T, D]
   int64_t h_sb, h_st;
   float* lam;              // [B, T, L] or null
+  // K/V mode (kv_k != null): the input is Y = X [Wk ; Wv]^T ([B, T, D] with
+  // D = 2 * Hkv * 128), and the blend of Y and its EMA, plus kv_bias, with
+  // rotate-half RoPE on the K half, is stored head-split into kv_k / kv_v
+  // ([B, Hkv, Tcap, 128], strides kv_sb, kv_sh, kv_st) at token slot t + t_offset.
+  __nv_bfloat16* kv_k;
+  __nv_bfloat16* kv_v;
+  int64_t kv_sb, kv_sh, kv_st;
+  int t_offset;
+  const float* kv_bias;    // [D] or null
+  const float* rope_cos;   // [*, T, 128] fp32 or null
+  const float* rope_sin;
+  int64_t rope_sb, rope_st;
   const float* ema_init;   // [B, D] fp32 EMA state before token 0 (null: zero), scan mode only
   float* ema_final;        // [B, D] fp32 EMA state after token T-1 (null: not written)
   uint32_t* ticket;
@@ -358,7 +370,47 @@ __global__ void __launch_bounds__(kThreads, FMKA_SCAN_MINB) route_ema_blend_kern
       *reinterpret_cast<float4*>(f) = make_float4(st[0], st[1], st[2], st[3]);
       *reinterpret_cast<float4*>(f + 4) = make_float4(st[4], st[5], st[6], st[7]);
     }
-    if (ch_ok && t < p.T) {
+    if (p.kv_k != nullptr) {
+      // K/V of the blend: bias, then RoPE on the K half. Channel d0 + c of a
+      // 128-dim head pairs with d0 + c -/+ 64, which lives 8 lanes away.
+      const int nk = p.D >> 1;  // K channels
+      const bool is_k = d0 < nk;
+      if (p.kv_bias != nullptr && ch_ok) {
+        const float4 b0 = *reinterpret_cast<const float4*>(p.kv_bias + d0);
+        const float4 b1 = *reinterpret_cast<const float4*>(p.kv_bias + d0 + 4);
+        o[0] += b0.x; o[1] += b0.y; o[2] += b0.z; o[3] += b0.w;
+        o[4] += b1.x; o[5] += b1.y; o[6] += b1.z; o[7] += b1.w;
+      }
+      const int dim = d0 & 127;  // position of this lane's 8 channels in their head
+      if (p.rope_cos != nullptr) {
+        float partner[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) partner[c] = __shfl_xor_sync(0xffffffffu, o[c], 8);
+        if (is_k && ch_ok && t < p.T) {
+          const int64_t roff = (int64_t)b * p.rope_sb + (int64_t)t * p.rope_st + dim;
+          const float sign = dim < 64 ? -1.f : 1.f;  // rotate_half: (-x2, x1)
+          const float4 c0 = *reinterpret_cast<const float4*>(p.rope_cos + roff);
+          const float4 c1 = *reinterpret_cast<const float4*>(p.rope_cos + roff + 4);
+          const float4 s0 = *reinterpret_cast<const float4*>(p.rope_sin + roff);
+          const float4 s1 = *reinterpret_cast<const float4*>(p.rope_sin + roff + 4);
+          const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+          for (int c = 0; c < 8; ++c) o[c] = o[c] * cs[c] + sign * partner[c] * sn[c];
+        }
+      }
+      if (ch_ok && t < p.T) {
+        const int head = (is_k ? d0 : d0 - nk) >> 7;
+        __nv_bfloat16* dst = (is_k ? p.kv_k : p.kv_v) + (int64_t)b * p.kv_sb + (int64_t)head * p.kv_sh +
+                             (int64_t)(t + p.t_offset) * p.kv_st + dim;
+        uint4 w;
+        w.x = pack_bf16x2(o[0], o[1]);
+        w.y = pack_bf16x2(o[2], o[3]);
+        w.z = pack_bf16x2(o[4], o[5]);
+        w.w = pack_bf16x2(o[6], o[7]);
+        *reinterpret_cast<uint4*>(dst) = w;
+      }
+    } else if (ch_ok && t < p.T) {
       uint4 w;
       w.x = pack_bf16x2(o[0], o[1]);
       w.y = pack_bf16x2(o[2], o[3]);
@@ -386,12 +438,25 @@ size_t route_ema_blend_flag_bytes(int B, int T, int D) {
   return (size_t)(((nrec * 4 + 256 + 255) / 256) * 256);
 }
 
+// K/V output of the blend (see ScanParams); null kv_k keeps the H output.
+struct KvOut {
+  __nv_bfloat16* k = nullptr;
+  __nv_bfloat16* v = nullptr;
+  int64_t sb = 0, sh = 0, st = 0;
+  int t_offset = 0;
+  const float* bias = nullptr;
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+  int64_t rope_sb = 0, rope_st = 0;
+};
+
 int launch_route_ema_blend(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, const __nv_bfloat16* l2,
                            int64_t l2_sb, int64_t l2_st, const float* logits,
                            const float* b2, const float* gate, int L, const __nv_bfloat16* l3, int64_t l3_sb,
                            int64_t l3_st, int T3, float beta, int B, int T, int D, __nv_bfloat16* h,
                            int64_t h_sb, int64_t h_st, float* lam, void* workspace, size_t workspace_bytes,
-                           bool clear_flags, cudaStream_t stream, const float* ema_init, float* ema_final) {
+                           bool clear_flags, cudaStream_t stream, const float* ema_init, float* ema_final,
+                           const KvOut* kv = nullptr) {
   if (B <= 0 || T <= 0 || D <= 0) return set_error(kErrInvalidArgument, "route_ema_blend: empty shape");
   if (l2 != nullptr && (ema_init != nullptr || ema_final != nullptr))
     return set_error(kErrInvalidArgument, "route_ema_blend: an EMA state needs the scan (no given L2)");
@@ -443,6 +508,26 @@ int launch_route_ema_blend(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, c
   p.lam = lam;
   p.ema_init = ema_init;
   p.ema_final = ema_final;
+  p.kv_k = nullptr;
+  p.kv_v = nullptr;
+  p.kv_bias = nullptr;
+  p.rope_cos = p.rope_sin = nullptr;
+  p.kv_sb = p.kv_sh = p.kv_st = 0;
+  p.t_offset = 0;
+  p.rope_sb = p.rope_st = 0;
+  if (kv != nullptr) {
+    p.kv_k = kv->k;
+    p.kv_v = kv->v;
+    p.kv_sb = kv->sb;
+    p.kv_sh = kv->sh;
+    p.kv_st = kv->st;
+    p.t_offset = kv->t_offset;
+    p.kv_bias = kv->bias;
+    p.rope_cos = kv->rope_cos;
+    p.rope_sin = kv->rope_sin;
+    p.rope_sb = kv->rope_sb;
+    p.rope_st = kv->rope_st;
+  }
   p.nds = (D + kSlice - 1) / kSlice;
   p.nchunks = (T + kChunkT - 1) / kChunkT;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -461,6 +546,45 @@ int launch_route_ema_blend(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, c
   if (grid > 0x7FFFFFFF) return set_error(kErrUnsupported, "route_ema_blend: problem too large");
   route_ema_blend_kernel<<<(unsigned)grid, kThreads, 0, stream>>>(p);
   return check_cuda(cudaGetLastError(), "route_ema_blend launch");
+}
+
+// Stage 1 on the projected memory: Y = X [Wk ; Wv]^T (bf16 [B, T, 2*Hkv*128])
+// in, K/V out. Because the EMA runs along tokens and the projection along
+// channels, EMA(X) Wk^T = EMA(X Wk^T); and since the gate sums to one, the
+// bias can be added after the blend: K = lam0 (X Wk^T) + lam1 EMA(X Wk^T) + bk
+// equals (lam0 X + lam1 EMA(X)) Wk^T + bk, the reference's k_proj of the fused
+// memory (mka/hf/attention.py:105-111). Two levels only.
+int launch_route_ema_blend_kv(const __nv_bfloat16* y, int64_t y_sb, int64_t y_st, const float* logits, const float* b2,
+                              float beta, int B, int T, int Hkv, const float* bias, __nv_bfloat16* k_out,
+                              __nv_bfloat16* v_out, int64_t kv_sb, int64_t kv_sh, int64_t kv_st, int t_offset,
+                              const float* rope_cos, const float* rope_sin, int64_t rope_sb, int64_t rope_st,
+                              float* lam, const float* ema_init, float* ema_final, void* workspace,
+                              size_t workspace_bytes, cudaStream_t stream) {
+  if (Hkv <= 0) return set_error(kErrInvalidArgument, "route_ema_blend_kv: no kv heads");
+  if (k_out == nullptr || v_out == nullptr || logits == nullptr)
+    return set_error(kErrInvalidArgument, "route_ema_blend_kv: null pointer");
+  if ((kv_st % 8) || (kv_sh % 8) || (kv_sb % 8) || t_offset < 0 ||
+      ((reinterpret_cast<uintptr_t>(k_out) | reinterpret_cast<uintptr_t>(v_out)) & 15u))
+    return set_error(kErrInvalidArgument, "route_ema_blend_kv: K/V need 16-byte aligned rows");
+  if ((rope_cos == nullptr) != (rope_sin == nullptr))
+    return set_error(kErrInvalidArgument, "route_ema_blend_kv: pass both RoPE tables or neither");
+  if (bias != nullptr && (reinterpret_cast<uintptr_t>(bias) & 15u))
+    return set_error(kErrInvalidArgument, "route_ema_blend_kv: bias must be 16-byte aligned");
+  KvOut kv;
+  kv.k = k_out;
+  kv.v = v_out;
+  kv.sb = kv_sb;
+  kv.sh = kv_sh;
+  kv.st = kv_st;
+  kv.t_offset = t_offset;
+  kv.bias = bias;
+  kv.rope_cos = rope_cos;
+  kv.rope_sin = rope_sin;
+  kv.rope_sb = rope_sb;
+  kv.rope_st = rope_st;
+  return launch_route_ema_blend(y, y_sb, y_st, nullptr, 0, 0, logits, b2, nullptr, 2, nullptr, 0, 0, 0, beta, B, T,
+                                2 * Hkv * 128, nullptr, 0, 0, lam, workspace, workspace_bytes, true, stream, ema_init,
+                                ema_final, &kv);
 }
 
 // ---------------------------------------------------------------------------

@@ -7,8 +7,9 @@ buffer pair per attention layer; the K/V projection kernel writes the new
 tokens straight into their slots and attention reads the valid prefix in place.
 Pass it as `past_key_value` to HFFastMKAAttention.
 
-With `carry_ema=True` the cache also keeps each layer's EMA (L2) state, fp32
-[B, D], so that the L2 memory continues across calls instead of restarting at
+With `carry_ema=True` the cache also keeps each layer's EMA (L2) state in
+fp32 (of x [Wk ; Wv]^T for two levels, [B, 2*Hkv*128]; of x for three,
+[B, D]), so that the L2 memory continues across calls instead of restarting at
 zero on every call as the reference does (session_memory.py:17-21): a decode
 step then sees the same L2 as the reference's prefill of the whole sequence.
 """

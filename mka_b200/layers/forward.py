@@ -4,10 +4,16 @@ beyond what the data flow needs.
   1. qr_proj          q = x Wq^T (+bq) -> head-split [B,Hq,T,128] (+RoPE), and the
                       router hidden act(x (W1 Wq)^T + b1') reduced against W2 into
                       per-token gate logits, in the GEMM epilogue
-  2. route_ema_blend  lam = softmax(logits + b2); L2 = prefix EMA of x; fused
-                      H = lam0 x + lam1 L2 (+ lam2 L3); H written once
-  3. kv_proj          [K | V] = H [Wk ; Wv]^T (+bias) -> head-split K/V (+RoPE on K),
-                      written straight into the K/V buffer after any cached prefix
+  two levels (L1 + L2):
+  2. kv_proj          y = x [Wk ; Wv]^T (bf16, 2*Hkv*128 channels)
+  3. route_ema_blend  lam = softmax(logits + b2); K/V = lam0 y + lam1 EMA(y)
+                      (+bias, RoPE on K) -> head-split K/V, written straight into
+                      the K/V buffer after any cached prefix. This is the
+                      reference's projection of lam0 x + lam1 EMA(x) in the
+                      commuted order (EMA along tokens, projection along channels)
+  three levels (L1 + L2 + L3):
+  2. route_ema_blend  H = lam0 x + lam1 EMA(x) + lam2 L3, written once
+  3. kv_proj          [K | V] = H [Wk ; Wv]^T (+bias) -> head-split K/V (+RoPE on K)
   4. attention        tcgen05 causal flash attention (prefill) or split-KV decode
                       (one new token), output [B, T, Hq, 128] and LSE
   5. o_proj           out = O Wo^T (+bo)
@@ -48,9 +54,11 @@ def fastmka_forward(x: torch.Tensor, W: PreparedWeights, num_heads: int, num_kv_
     kv_update: alternatively a callable given this call's new (k, v)
              [B, Hkv, T, 128] (post-RoPE) that returns the full (k, v) to attend
              to, e.g. a transformers Cache's update(k, v, layer_idx).
-    ema_state / ema_out: fp32 [B, D] EMA state before this call's first token
-             (None: zero, the reference's restart) and a buffer for the state
-             after its last token, to carry the L2 memory across calls.
+    ema_state / ema_out: fp32 EMA state before this call's first token (None:
+             zero, the reference's restart) and a buffer for the state after its
+             last token, to carry the L2 memory across calls. With two levels
+             the scan runs on x [Wk ; Wv]^T, so the state is [B, 2*Hkv*128];
+             with three it is the state of EMA(x), [B, D].
     Returns dict(out [B,T,D] bf16, k, v, lam [B,T,L] fp32, lse).
     """
     def mark(name):
@@ -83,45 +91,12 @@ def fastmka_forward(x: torch.Tensor, W: PreparedWeights, num_heads: int, num_kv_
     q, logits = ops.qr_proj(xb.view(B * T, D), W.w_qr, W.b_qr, B, T, num_heads, W.router_hidden, W.w2, L,
                             W.act, rope=rope)
     done()
-    # 2. gate + EMA + blend
-    l3 = None
-    if use_l3:
-        if l3_memory is None:
-            l3 = torch.zeros((B, 1, D), dtype=torch.bfloat16, device=x.device)
-        else:
-            l3 = l3_memory if l3_memory.dtype == torch.bfloat16 else l3_memory.to(torch.bfloat16)
-            if l3.shape[0] != B or l3.shape[2] != D:
-                raise RuntimeError("l3_memory must be [B, T3, D]")
-    mark("route_ema_blend")
-    h, lam = ops.route_ema_blend(xb, beta, logits=logits, b2=W.b2, levels=L, l3=l3, ema_state=ema_state,
-                                 ema_out=ema_out)
-    done()
-    mark("kv_proj")
-    # 3. K/V of the fused memory
-    if kv_out is not None:
-        kc, vc = kv_out
-        tp = int(past_len or 0)
-        if tp + T > kc.shape[2]:
-            raise RuntimeError("preallocated K/V cache is full")
-        ops.kv_proj(h.view(B * T, D), W.w_kv, W.b_kv, B, T, num_kv_heads, rope=rope, k_out=kc, v_out=vc,
-                    t_offset=tp)
-        k_tot, v_tot = kc[:, :, : tp + T], vc[:, :, : tp + T]
-    elif past is not None:
-        pk, pv = past
-        tp = pk.shape[2]
-        k_tot = torch.empty((B, num_kv_heads, tp + T, HEAD_DIM), dtype=torch.bfloat16, device=x.device)
-        v_tot = torch.empty_like(k_tot)
-        k_tot[:, :, :tp].copy_(pk)
-        v_tot[:, :, :tp].copy_(pv)
-        ops.kv_proj(h.view(B * T, D), W.w_kv, W.b_kv, B, T, num_kv_heads, rope=rope, k_out=k_tot, v_out=v_tot,
-                    t_offset=tp)
+    if L == 2:
+        k_tot, v_tot, lam = _kv_two_levels(xb, logits, W, B, T, D, num_kv_heads, beta, rope, past, kv_out,
+                                           past_len, kv_update, ema_state, ema_out, mark, done)
     else:
-        k_tot, v_tot = ops.kv_proj(h.view(B * T, D), W.w_kv, W.b_kv, B, T, num_kv_heads, rope=rope)
-        if kv_update is not None:
-            k_tot, v_tot = kv_update(k_tot, v_tot)
-            if k_tot.dtype != torch.bfloat16 or v_tot.dtype != torch.bfloat16:
-                raise RuntimeError("the K/V returned by kv_update must be bf16")
-    done()
+        k_tot, v_tot, lam = _kv_three_levels(xb, logits, W, B, T, D, num_kv_heads, beta, rope, past, kv_out,
+                                             past_len, kv_update, ema_state, ema_out, l3_memory, mark, done)
     # 4. attention
     mark("attention")
     if T == 1 and k_tot.shape[2] > 1:
@@ -135,3 +110,76 @@ def fastmka_forward(x: torch.Tensor, W: PreparedWeights, num_heads: int, num_kv_
     out = ops.gemm(o.view(B * T, num_heads * HEAD_DIM), W.w_o, W.b_o).view(B, T, D)
     done()
     return {"out": out, "k": k_tot, "v": v_tot, "lam": lam, "lse": lse, "q": q}
+
+
+def _kv_buffers(B, T, num_kv_heads, past, kv_out, past_len, device):
+    """Where this call's K/V land: (k_target, v_target, t_offset, k_total, v_total);
+    targets None means fresh [B, Hkv, T, 128] buffers made by the kernel wrapper."""
+    if kv_out is not None:
+        kc, vc = kv_out
+        tp = int(past_len or 0)
+        if tp + T > kc.shape[2]:
+            raise RuntimeError("preallocated K/V cache is full")
+        return kc, vc, tp, kc[:, :, : tp + T], vc[:, :, : tp + T]
+    if past is not None:
+        pk, pv = past
+        tp = pk.shape[2]
+        k_tot = torch.empty((B, num_kv_heads, tp + T, HEAD_DIM), dtype=torch.bfloat16, device=device)
+        v_tot = torch.empty_like(k_tot)
+        k_tot[:, :, :tp].copy_(pk)
+        v_tot[:, :, :tp].copy_(pv)
+        return k_tot, v_tot, tp, k_tot, v_tot
+    return None, None, 0, None, None
+
+
+def _finish_kv(k_new, v_new, k_tot, v_tot, kv_update):
+    if k_tot is None:
+        k_tot, v_tot = k_new, v_new
+        if kv_update is not None:
+            k_tot, v_tot = kv_update(k_tot, v_tot)
+            if k_tot.dtype != torch.bfloat16 or v_tot.dtype != torch.bfloat16:
+                raise RuntimeError("the K/V returned by kv_update must be bf16")
+    return k_tot, v_tot
+
+
+def _kv_two_levels(xb, logits, W, B, T, D, num_kv_heads, beta, rope, past, kv_out, past_len, kv_update,
+                   ema_state, ema_out, mark, done):
+    """Two levels: y = x [Wk ; Wv]^T, then one scan over y's 2*Hkv*128 channels
+    writes K/V = lam0 y + lam1 EMA(y) + bias (RoPE on K). Equal to projecting
+    the blend lam0 x + lam1 EMA(x) (fastmka.py:94-99, hf/attention.py:105-111):
+    the EMA runs along tokens and the projection along channels, and the gate
+    sums to one; the scan then touches 2*Hkv*128 channels instead of d_model."""
+    kt, vt, tp, k_tot, v_tot = _kv_buffers(B, T, num_kv_heads, past, kv_out, past_len, xb.device)
+    mark("kv_proj")
+    y = ops.gemm(xb.view(B * T, D), W.w_kv)
+    done()
+    mark("route_ema_blend")
+    k_new, v_new, lam = ops.route_ema_blend_kv(y, beta, logits, W.b2, B, T, num_kv_heads, bias=W.b_kv, rope=rope,
+                                               k_out=kt, v_out=vt, t_offset=tp, ema_state=ema_state,
+                                               ema_out=ema_out)
+    done()
+    k_tot, v_tot = _finish_kv(k_new, v_new, k_tot, v_tot, kv_update)
+    return k_tot, v_tot, lam
+
+
+def _kv_three_levels(xb, logits, W, B, T, D, num_kv_heads, beta, rope, past, kv_out, past_len, kv_update,
+                     ema_state, ema_out, l3_memory, mark, done):
+    """Three levels: the blend H = lam0 x + lam1 EMA(x) + lam2 L3 over d_model,
+    then the K/V projection of H (+ RoPE on K)."""
+    if l3_memory is None:
+        l3 = torch.zeros((B, 1, D), dtype=torch.bfloat16, device=xb.device)
+    else:
+        l3 = l3_memory if l3_memory.dtype == torch.bfloat16 else l3_memory.to(torch.bfloat16)
+        if l3.shape[0] != B or l3.shape[2] != D:
+            raise RuntimeError("l3_memory must be [B, T3, D]")
+    mark("route_ema_blend")
+    h, lam = ops.route_ema_blend(xb, beta, logits=logits, b2=W.b2, levels=3, l3=l3, ema_state=ema_state,
+                                 ema_out=ema_out)
+    done()
+    kt, vt, tp, k_tot, v_tot = _kv_buffers(B, T, num_kv_heads, past, kv_out, past_len, xb.device)
+    mark("kv_proj")
+    k_new, v_new = ops.kv_proj(h.view(B * T, D), W.w_kv, W.b_kv, B, T, num_kv_heads, rope=rope, k_out=kt,
+                               v_out=vt, t_offset=tp)
+    done()
+    k_tot, v_tot = _finish_kv(k_new, v_new, k_tot, v_tot, kv_update)
+    return k_tot, v_tot, lam

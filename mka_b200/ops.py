@@ -239,6 +239,48 @@ def route_ema_blend(x: torch.Tensor, beta: float, logits: Optional[torch.Tensor]
     return h, lam
 
 
+def route_ema_blend_kv(y: torch.Tensor, beta: float, logits: torch.Tensor, b2: Optional[torch.Tensor], B: int,
+                       T: int, num_kv_heads: int, bias: Optional[torch.Tensor] = None,
+                       rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+                       k_out: Optional[torch.Tensor] = None, v_out: Optional[torch.Tensor] = None,
+                       t_offset: int = 0, want_lam: bool = True, ema_state: Optional[torch.Tensor] = None,
+                       ema_out: Optional[torch.Tensor] = None):
+    """K/V of the two-level route blend from y = x [Wk ; Wv]^T ([B*T, 2*Hkv*128] bf16).
+
+    K = lam0 * yk + lam1 * EMA(yk) + bk (then RoPE), V likewise: the reference's
+    k/v projection of lam0 * x + lam1 * EMA(x), in the commuted order (the EMA
+    runs along tokens, the projection along channels). Written head-split into
+    k_out / v_out ([B, Hkv, Tcap, 128]) at token slots [t_offset, t_offset + T).
+    ema_state / ema_out: fp32 [B, 2*Hkv*128] states of EMA(y). Returns
+    (k_out, v_out, lam [B, T, 2] fp32 or None).
+    """
+    _check_cuda(y, logits, ema_state, ema_out)
+    _check_bf16(y)
+    N = 2 * num_kv_heads * HEAD_DIM
+    if y.dim() != 2 or y.shape[0] != B * T or y.shape[1] != N or y.stride(1) != 1:
+        raise RuntimeError(f"route_ema_blend_kv: y must be [B*T, {N}] with contiguous rows")
+    for name, t in (("ema_state", ema_state), ("ema_out", ema_out)):
+        if t is not None and (t.dtype != torch.float32 or tuple(t.shape) != (B, N) or not t.is_contiguous()):
+            raise RuntimeError(f"route_ema_blend_kv: {name} must be a contiguous fp32 [B, {N}] tensor")
+    if ema_state is not None and ema_out is not None and ema_state.data_ptr() == ema_out.data_ptr():
+        raise RuntimeError("route_ema_blend_kv: ema_state and ema_out must be different buffers")
+    if k_out is None:
+        k_out = torch.empty((B, num_kv_heads, T, HEAD_DIM), dtype=torch.bfloat16, device=y.device)
+    if v_out is None:
+        v_out = torch.empty_like(k_out)
+    if k_out.stride() != v_out.stride():
+        raise RuntimeError("route_ema_blend_kv: k and v outputs must share strides")
+    lam = torch.empty((B, T, 2), dtype=torch.float32, device=y.device) if want_lam else None
+    cos, sin, rsb, rst = _rope_args(rope, B, T)
+    ws_bytes = _lib.load().fmka_route_ema_blend_kv_workspace_size(B, T, num_kv_heads)
+    ws = _WS.get(y.device, ws_bytes)
+    _lib.call("fmka_route_ema_blend_kv", y.data_ptr(), T * y.stride(0), y.stride(0), _ptr(logits.contiguous()),
+              _ptr(_f32(b2)), float(beta), B, T, num_kv_heads, _ptr(_f32(bias)), k_out.data_ptr(), v_out.data_ptr(),
+              k_out.stride(0), k_out.stride(1), k_out.stride(2), t_offset, _ptr(cos), _ptr(sin), rsb, rst,
+              _ptr(lam), _ptr(ema_state), _ptr(ema_out), _ptr(ws), ws_bytes, _stream(y))
+    return k_out, v_out, lam
+
+
 def causal_prefix_ema(x: torch.Tensor, beta: float = 0.9, state: Optional[torch.Tensor] = None,
                       state_out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """L2[t] = beta * L2[t-1] + (1 - beta) * x[t] with L2[-1] = 0 (session_memory.py:6-22),

@@ -147,6 +147,41 @@ def test_causal_prefix_ema_op(ops):
     assert _rel(out, _ref_ema(x.float(), 0.9)) < 1e-2
 
 
+@pytest.mark.parametrize("B,T,Hkv,rope,off", [(2, 300, 4, True, 0), (3, 65, 1, True, 7), (1, 1, 2, False, 5),
+                                          (2, 130, 8, True, 0), (4, 64, 4, False, 0)])
+def test_route_ema_blend_kv(ops, B, T, Hkv, rope, off):
+    """Two-level stage 1 on y = x [Wk ; Wv]^T: K/V = lam0 y + lam1 EMA(y) + bias,
+    RoPE on K, head-split at token slot t + off."""
+    N = 2 * Hkv * 128
+    g = torch.Generator(device="cuda").manual_seed(B * 1000 + T)
+    y = torch.randn(B * T, N, device="cuda", generator=g).bfloat16()
+    logits = torch.randn(B * T, 2, device="cuda", generator=g)
+    b2 = torch.randn(2, device="cuda", generator=g)
+    bias = torch.randn(N, device="cuda", generator=g) * 0.1
+    cs = None
+    if rope:
+        ang = torch.rand(B, T, 128, device="cuda", generator=g) * 6
+        cs = (ang.cos(), ang.sin())
+    kc = torch.zeros(B, Hkv, T + off + 3, 128, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    _, _, lam = ops.route_ema_blend_kv(y, 0.9, logits, b2, B, T, Hkv, bias=bias, rope=cs, k_out=kc, v_out=vc,
+                                       t_offset=off)
+    lam_ref = torch.softmax(logits + b2, -1).view(B, T, 2)
+    yf = y.float().view(B, T, N)
+    blend = lam_ref[..., 0:1] * yf + lam_ref[..., 1:2] * _ref_ema(yf, 0.9) + bias
+    kf = blend[..., : N // 2].reshape(B, T, Hkv, 128).transpose(1, 2)
+    vf = blend[..., N // 2:].reshape(B, T, Hkv, 128).transpose(1, 2)
+    if rope:
+        cos, sin = cs[0][:, None], cs[1][:, None]
+        kf = kf * cos + torch.cat([-kf[..., 64:], kf[..., :64]], -1) * sin
+    assert ops.device_status() == 0
+    assert _rel(lam, lam_ref) < 1e-5
+    assert _rel(kc[:, :, off:off + T], kf) < 1e-2
+    assert _rel(vc[:, :, off:off + T], vf) < 1e-2
+    assert kc[:, :, :off].abs().max().item() == 0 if off else True
+    assert kc[:, :, off + T:].abs().max().item() == 0 and vc[:, :, off + T:].abs().max().item() == 0
+
+
 @pytest.mark.parametrize("T1,T2,D,beta", [(173, 127, 3584, 0.9), (64, 1, 136, 0.99), (1, 1, 264, 0.5),
                                          (700, 45, 520, 0.999)])
 def test_ema_carried_state(ops, T1, T2, D, beta):
