@@ -171,7 +171,7 @@ FMKA_API int fmka_route_ema_blend_state(const void* x, int64_t x_sb, int64_t x_s
                                         float* ema_final, void* workspace, size_t workspace_bytes,
                                         fmka_stream_t stream);
 
-/* fmka_route_ema_blend_kv: stage 1 on the projected memory, for two levels.
+/* fmka_route_ema_blend_kv: stage 1 on the projected memory.
  * Input y = x [Wk ; Wv]^T (bf16 [B, T, 2*Hkv*128], rows y_st apart, batches
  * y_sb; from fmka_gemm_bf16 without bias). Output the reference's k_proj /
  * v_proj of the fused memory (mka/hf/attention.py:97-119,
@@ -182,12 +182,16 @@ FMKA_API int fmka_route_ema_blend_state(const void* x, int64_t x_sb, int64_t x_s
  *   [*, T, 128], may be NULL), and V likewise without RoPE,
  * which equals projecting lam0 * x + lam1 * EMA(x) because the EMA (along
  * tokens) commutes with the projection (along channels) and the gate sums to
- * one. The scan runs over 2*Hkv*128 channels instead of d_model. lam (fp32
- * [B, T, 2]), ema_init / ema_final (fp32 [B, 2*Hkv*128], the state of
+ * one. The scan runs over 2*Hkv*128 channels instead of d_model. A third
+ * level is given as y3 = l3 [Wk ; Wv]^T ([B, T3, 2*Hkv*128] at strides
+ * (y3_sb, y3_st), row t uses min(t, T3 - 1), y3_st may be 0) and adds
+ * lam2 * y3 (logits and b2 then have 3 levels); y3 = NULL for two levels.
+ * lam (fp32 [B, T, L]), ema_init / ema_final (fp32 [B, 2*Hkv*128], the state of
  * EMA(y), as for fmka_route_ema_blend_state) may be NULL. */
 FMKA_API size_t fmka_route_ema_blend_kv_workspace_size(int B, int T, int Hkv);
 FMKA_API int fmka_route_ema_blend_kv(const void* y, int64_t y_sb, int64_t y_st, const float* logits,
-                                     const float* b2, float beta, int B, int T, int Hkv, const float* bias,
+                                     const float* b2, const void* y3, int64_t y3_sb, int64_t y3_st, int T3,
+                                     float beta, int B, int T, int Hkv, const float* bias,
                                      void* k_out, void* v_out, int64_t kv_sb, int64_t kv_sh, int64_t kv_st,
                                      int t_offset, const float* rope_cos, const float* rope_sin, int64_t rope_sb,
                                      int64_t rope_st, float* lam, const float* ema_init, float* ema_final,

@@ -39,7 +39,7 @@ _SIGNATURES = {
     "fmka_route_ema_blend_state": (_I, [_P, _L, _L, _P, _P, _P, _I, _P, _L, _L, _I, _F, _I, _I, _I,
                                         _P, _L, _L, _P, _P, _P, _P, c_size_t, _P]),
     "fmka_route_ema_blend_kv_workspace_size": (c_size_t, [_I, _I, _I]),
-    "fmka_route_ema_blend_kv": (_I, [_P, _L, _L, _P, _P, _F, _I, _I, _I, _P, _P, _P, _L, _L, _L, _I, _P, _P,
+    "fmka_route_ema_blend_kv": (_I, [_P, _L, _L, _P, _P, _P, _L, _L, _I, _F, _I, _I, _I, _P, _P, _P, _L, _L, _L, _I, _P, _P,
                                      _L, _L, _P, _P, _P, _P, c_size_t, _P]),
     "fmka_route_blend": (_I, [_P, _L, _L, _P, _L, _L, _P, _L, _L, _I, _P, _I, _I, _I, _I, _P, _L, _L, _P]),
     "fmka_attn_fwd_prefill": (_I, [_P, _L, _L, _L, _P, _P, _L, _L, _L, _P, _L, _L, _L, _P, _L, _L,

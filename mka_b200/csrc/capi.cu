@@ -25,7 +25,7 @@ int launch_route_ema_blend(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, c
                            bool clear_flags, cudaStream_t stream, const float* ema_init = nullptr,
                            float* ema_final = nullptr, const struct KvOut* kv = nullptr);
 int launch_route_ema_blend_kv(const __nv_bfloat16* y, int64_t y_sb, int64_t y_st, const float* logits, const float* b2,
-                              float beta, int B, int T, int Hkv, const float* bias, __nv_bfloat16* k_out,
+                              const __nv_bfloat16* y3, int64_t y3_sb, int64_t y3_st, int T3, float beta, int B, int T, int Hkv, const float* bias, __nv_bfloat16* k_out,
                               __nv_bfloat16* v_out, int64_t kv_sb, int64_t kv_sh, int64_t kv_st, int t_offset,
                               const float* rope_cos, const float* rope_sin, int64_t rope_sb, int64_t rope_st,
                               float* lam, const float* ema_init, float* ema_final, void* workspace,
@@ -384,7 +384,7 @@ size_t fmka_route_ema_blend_kv_workspace_size(int B, int T, int Hkv) {
 }
 
 int fmka_route_ema_blend_kv(const void* y, int64_t y_sb, int64_t y_st, const float* logits, const float* b2,
-                            float beta, int B, int T, int Hkv, const float* bias, void* k_out, void* v_out,
+                            const void* y3, int64_t y3_sb, int64_t y3_st, int T3, float beta, int B, int T, int Hkv, const float* bias, void* k_out, void* v_out,
                             int64_t kv_sb, int64_t kv_sh, int64_t kv_st, int t_offset, const float* rope_cos,
                             const float* rope_sin, int64_t rope_sb, int64_t rope_st, float* lam,
                             const float* ema_init, float* ema_final, void* workspace, size_t workspace_bytes,
@@ -393,7 +393,8 @@ int fmka_route_ema_blend_kv(const void* y, int64_t y_sb, int64_t y_st, const flo
   if (!std::isfinite(beta)) return set_error(kErrInvalidArgument, "route_ema_blend_kv: beta must be finite");
   if (ema_init != nullptr && ema_init == ema_final)
     return set_error(kErrInvalidArgument, "route_ema_blend_kv: ema_init and ema_final must not alias");
-  return launch_route_ema_blend_kv(bf(y), y_sb, y_st, logits, b2, beta, B, T, Hkv, bias, bfw(k_out), bfw(v_out),
+  if (y3 != nullptr && T3 < 1) return set_error(kErrInvalidArgument, "route_ema_blend_kv: y3 needs T3 >= 1");
+  return launch_route_ema_blend_kv(bf(y), y_sb, y_st, logits, b2, bf(y3), y3_sb, y3_st, T3, beta, B, T, Hkv, bias, bfw(k_out), bfw(v_out),
                                    kv_sb, kv_sh, kv_st, t_offset, rope_cos, rope_sin, rope_sb, rope_st, lam,
                                    ema_init, ema_final, workspace, workspace_bytes, as_stream(stream));
 }

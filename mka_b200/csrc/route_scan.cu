@@ -553,8 +553,10 @@ int launch_route_ema_blend(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, c
 // channels, EMA(X) Wk^T = EMA(X Wk^T); and since the gate sums to one, the
 // bias can be added after the blend: K = lam0 (X Wk^T) + lam1 EMA(X Wk^T) + bk
 // equals (lam0 X + lam1 EMA(X)) Wk^T + bk, the reference's k_proj of the fused
-// memory (mka/hf/attention.py:105-111). Two levels only.
+// memory (mka/hf/attention.py:105-111). With a third level, y3 = L3 [Wk ; Wv]^T
+// ([B, T3, 2*Hkv*128], row t uses min(t, T3 - 1)) adds lam2 * y3.
 int launch_route_ema_blend_kv(const __nv_bfloat16* y, int64_t y_sb, int64_t y_st, const float* logits, const float* b2,
+                              const __nv_bfloat16* y3, int64_t y3_sb, int64_t y3_st, int T3,
                               float beta, int B, int T, int Hkv, const float* bias, __nv_bfloat16* k_out,
                               __nv_bfloat16* v_out, int64_t kv_sb, int64_t kv_sh, int64_t kv_st, int t_offset,
                               const float* rope_cos, const float* rope_sin, int64_t rope_sb, int64_t rope_st,
@@ -582,9 +584,10 @@ int launch_route_ema_blend_kv(const __nv_bfloat16* y, int64_t y_sb, int64_t y_st
   kv.rope_sin = rope_sin;
   kv.rope_sb = rope_sb;
   kv.rope_st = rope_st;
-  return launch_route_ema_blend(y, y_sb, y_st, nullptr, 0, 0, logits, b2, nullptr, 2, nullptr, 0, 0, 0, beta, B, T,
-                                2 * Hkv * 128, nullptr, 0, 0, lam, workspace, workspace_bytes, true, stream, ema_init,
-                                ema_final, &kv);
+  const int L = y3 != nullptr ? 3 : 2;
+  return launch_route_ema_blend(y, y_sb, y_st, nullptr, 0, 0, logits, b2, nullptr, L, y3, y3_sb, y3_st, T3, beta, B,
+                                T, 2 * Hkv * 128, nullptr, 0, 0, lam, workspace, workspace_bytes, true, stream,
+                                ema_init, ema_final, &kv);
 }
 
 // ---------------------------------------------------------------------------

@@ -122,8 +122,8 @@ class HFFastMKAAttention(nn.Module):
                 kc, vc = cache.layer(self)
                 ema_in = ema_out = None
                 if cache.carry_ema:
-                    # the state of EMA(x [Wk ; Wv]^T) for two levels, of EMA(x) for three
-                    width = hidden_states.shape[2] if self.use_l3 else 2 * self.num_key_value_heads * self.head_dim
+                    # the state of EMA(x [Wk ; Wv]^T), the space the layer's scan runs in
+                    width = 2 * self.num_key_value_heads * self.head_dim
                     ema_in, ema_out = cache.ema_buffers(self, width, hidden_states.device)
                 r = fastmka_forward(hidden_states, W, self.num_heads, self.num_key_value_heads, self.ema_beta,
                                     self.use_l3, l3_memory=l3_memory, rope=rope, kv_out=(kc, vc),

@@ -8,8 +8,8 @@ tokens straight into their slots and attention reads the valid prefix in place.
 Pass it as `past_key_value` to HFFastMKAAttention.
 
 With `carry_ema=True` the cache also keeps each layer's EMA (L2) state in
-fp32 (of x [Wk ; Wv]^T for two levels, [B, 2*Hkv*128]; of x for three,
-[B, D]), so that the L2 memory continues across calls instead of restarting at
+fp32 (that of x [Wk ; Wv]^T, [B, 2*Hkv*128], the space the layer's scan runs
+in), so that the L2 memory continues across calls instead of restarting at
 zero on every call as the reference does (session_memory.py:17-21): a decode
 step then sees the same L2 as the reference's prefill of the whole sequence.
 """

@@ -4,16 +4,14 @@ beyond what the data flow needs.
   1. qr_proj          q = x Wq^T (+bq) -> head-split [B,Hq,T,128] (+RoPE), and the
                       router hidden act(x (W1 Wq)^T + b1') reduced against W2 into
                       per-token gate logits, in the GEMM epilogue
-  two levels (L1 + L2):
-  2. kv_proj          y = x [Wk ; Wv]^T (bf16, 2*Hkv*128 channels)
+  2. kv_proj          y = x [Wk ; Wv]^T (bf16, 2*Hkv*128 channels); with three
+                      levels also y3 = L3 [Wk ; Wv]^T
   3. route_ema_blend  lam = softmax(logits + b2); K/V = lam0 y + lam1 EMA(y)
-                      (+bias, RoPE on K) -> head-split K/V, written straight into
-                      the K/V buffer after any cached prefix. This is the
-                      reference's projection of lam0 x + lam1 EMA(x) in the
-                      commuted order (EMA along tokens, projection along channels)
-  three levels (L1 + L2 + L3):
-  2. route_ema_blend  H = lam0 x + lam1 EMA(x) + lam2 L3, written once
-  3. kv_proj          [K | V] = H [Wk ; Wv]^T (+bias) -> head-split K/V (+RoPE on K)
+                      (+ lam2 y3) (+bias, RoPE on K) -> head-split K/V, written
+                      straight into the K/V buffer after any cached prefix. This
+                      is the reference's projection of lam0 x + lam1 EMA(x)
+                      (+ lam2 L3) in the commuted order (EMA along tokens,
+                      projection along channels; the gate sums to one)
   4. attention        tcgen05 causal flash attention (prefill) or split-KV decode
                       (one new token), output [B, T, Hq, 128] and LSE
   5. o_proj           out = O Wo^T (+bo)
@@ -56,9 +54,8 @@ def fastmka_forward(x: torch.Tensor, W: PreparedWeights, num_heads: int, num_kv_
              to, e.g. a transformers Cache's update(k, v, layer_idx).
     ema_state / ema_out: fp32 EMA state before this call's first token (None:
              zero, the reference's restart) and a buffer for the state after its
-             last token, to carry the L2 memory across calls. With two levels
-             the scan runs on x [Wk ; Wv]^T, so the state is [B, 2*Hkv*128];
-             with three it is the state of EMA(x), [B, D].
+             last token, to carry the L2 memory across calls. The scan runs
+             on x [Wk ; Wv]^T, so the state is that of EMA(y), [B, 2*Hkv*128].
     Returns dict(out [B,T,D] bf16, k, v, lam [B,T,L] fp32, lse).
     """
     def mark(name):
@@ -91,12 +88,8 @@ def fastmka_forward(x: torch.Tensor, W: PreparedWeights, num_heads: int, num_kv_
     q, logits = ops.qr_proj(xb.view(B * T, D), W.w_qr, W.b_qr, B, T, num_heads, W.router_hidden, W.w2, L,
                             W.act, rope=rope)
     done()
-    if L == 2:
-        k_tot, v_tot, lam = _kv_two_levels(xb, logits, W, B, T, D, num_kv_heads, beta, rope, past, kv_out,
-                                           past_len, kv_update, ema_state, ema_out, mark, done)
-    else:
-        k_tot, v_tot, lam = _kv_three_levels(xb, logits, W, B, T, D, num_kv_heads, beta, rope, past, kv_out,
-                                             past_len, kv_update, ema_state, ema_out, l3_memory, mark, done)
+    k_tot, v_tot, lam = _kv_levels(xb, logits, W, B, T, D, num_kv_heads, beta, rope, past, kv_out, past_len,
+                                   kv_update, ema_state, ema_out, use_l3, l3_memory, mark, done)
     # 4. attention
     mark("attention")
     if T == 1 and k_tot.shape[2] > 1:
@@ -142,44 +135,38 @@ def _finish_kv(k_new, v_new, k_tot, v_tot, kv_update):
     return k_tot, v_tot
 
 
-def _kv_two_levels(xb, logits, W, B, T, D, num_kv_heads, beta, rope, past, kv_out, past_len, kv_update,
-                   ema_state, ema_out, mark, done):
-    """Two levels: y = x [Wk ; Wv]^T, then one scan over y's 2*Hkv*128 channels
-    writes K/V = lam0 y + lam1 EMA(y) + bias (RoPE on K). Equal to projecting
-    the blend lam0 x + lam1 EMA(x) (fastmka.py:94-99, hf/attention.py:105-111):
-    the EMA runs along tokens and the projection along channels, and the gate
-    sums to one; the scan then touches 2*Hkv*128 channels instead of d_model."""
+def project_l3(l3_memory: Optional[torch.Tensor], W: PreparedWeights, B: int, D: int, num_kv_heads: int,
+               device) -> torch.Tensor:
+    """y3 = L3 [Wk ; Wv]^T ([B, T3, 2*Hkv*128] bf16): the third memory level in
+    the projected space. No memory means the reference's zero L3
+    (hf/attention.py:100-102), projected to zero without a GEMM."""
+    n = 2 * num_kv_heads * HEAD_DIM
+    if l3_memory is None:
+        return torch.zeros((B, 1, n), dtype=torch.bfloat16, device=device)
+    l3 = l3_memory if l3_memory.dtype == torch.bfloat16 else l3_memory.to(torch.bfloat16)
+    if l3.dim() != 3 or l3.shape[0] != B or l3.shape[2] != D:
+        raise RuntimeError("l3_memory must be [B, T3, D]")
+    t3 = l3.shape[1]
+    return ops.gemm(l3.reshape(B * t3, D).contiguous(), W.w_kv).view(B, t3, n)
+
+
+def _kv_levels(xb, logits, W, B, T, D, num_kv_heads, beta, rope, past, kv_out, past_len, kv_update,
+               ema_state, ema_out, use_l3, l3_memory, mark, done):
+    """y = x [Wk ; Wv]^T, then one scan over y's 2*Hkv*128 channels writes
+    K/V = lam0 y + lam1 EMA(y) (+ lam2 y3) + bias (RoPE on K). Equal to
+    projecting the blend lam0 x + lam1 EMA(x) (+ lam2 L3) (fastmka.py:83-99,
+    hf/attention.py:97-111): the EMA runs along tokens and the projection along
+    channels, and the gate sums to one; the scan then touches 2*Hkv*128
+    channels instead of d_model."""
     kt, vt, tp, k_tot, v_tot = _kv_buffers(B, T, num_kv_heads, past, kv_out, past_len, xb.device)
     mark("kv_proj")
     y = ops.gemm(xb.view(B * T, D), W.w_kv)
+    y3 = project_l3(l3_memory, W, B, D, num_kv_heads, xb.device) if use_l3 else None
     done()
     mark("route_ema_blend")
     k_new, v_new, lam = ops.route_ema_blend_kv(y, beta, logits, W.b2, B, T, num_kv_heads, bias=W.b_kv, rope=rope,
                                                k_out=kt, v_out=vt, t_offset=tp, ema_state=ema_state,
-                                               ema_out=ema_out)
-    done()
-    k_tot, v_tot = _finish_kv(k_new, v_new, k_tot, v_tot, kv_update)
-    return k_tot, v_tot, lam
-
-
-def _kv_three_levels(xb, logits, W, B, T, D, num_kv_heads, beta, rope, past, kv_out, past_len, kv_update,
-                     ema_state, ema_out, l3_memory, mark, done):
-    """Three levels: the blend H = lam0 x + lam1 EMA(x) + lam2 L3 over d_model,
-    then the K/V projection of H (+ RoPE on K)."""
-    if l3_memory is None:
-        l3 = torch.zeros((B, 1, D), dtype=torch.bfloat16, device=xb.device)
-    else:
-        l3 = l3_memory if l3_memory.dtype == torch.bfloat16 else l3_memory.to(torch.bfloat16)
-        if l3.shape[0] != B or l3.shape[2] != D:
-            raise RuntimeError("l3_memory must be [B, T3, D]")
-    mark("route_ema_blend")
-    h, lam = ops.route_ema_blend(xb, beta, logits=logits, b2=W.b2, levels=3, l3=l3, ema_state=ema_state,
-                                 ema_out=ema_out)
-    done()
-    kt, vt, tp, k_tot, v_tot = _kv_buffers(B, T, num_kv_heads, past, kv_out, past_len, xb.device)
-    mark("kv_proj")
-    k_new, v_new = ops.kv_proj(h.view(B * T, D), W.w_kv, W.b_kv, B, T, num_kv_heads, rope=rope, k_out=kt,
-                               v_out=vt, t_offset=tp)
+                                               ema_out=ema_out, y3=y3)
     done()
     k_tot, v_tot = _finish_kv(k_new, v_new, k_tot, v_tot, kv_update)
     return k_tot, v_tot, lam

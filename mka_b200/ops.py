@@ -244,18 +244,28 @@ def route_ema_blend_kv(y: torch.Tensor, beta: float, logits: torch.Tensor, b2: O
                        rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
                        k_out: Optional[torch.Tensor] = None, v_out: Optional[torch.Tensor] = None,
                        t_offset: int = 0, want_lam: bool = True, ema_state: Optional[torch.Tensor] = None,
-                       ema_out: Optional[torch.Tensor] = None):
-    """K/V of the two-level route blend from y = x [Wk ; Wv]^T ([B*T, 2*Hkv*128] bf16).
+                       ema_out: Optional[torch.Tensor] = None, y3: Optional[torch.Tensor] = None):
+    """K/V of the route blend from y = x [Wk ; Wv]^T ([B*T, 2*Hkv*128] bf16).
 
     K = lam0 * yk + lam1 * EMA(yk) + bk (then RoPE), V likewise: the reference's
     k/v projection of lam0 * x + lam1 * EMA(x), in the commuted order (the EMA
     runs along tokens, the projection along channels). Written head-split into
     k_out / v_out ([B, Hkv, Tcap, 128]) at token slots [t_offset, t_offset + T).
-    ema_state / ema_out: fp32 [B, 2*Hkv*128] states of EMA(y). Returns
-    (k_out, v_out, lam [B, T, 2] fp32 or None).
+    ema_state / ema_out: fp32 [B, 2*Hkv*128] states of EMA(y). y3: the third
+    level projected, l3 [Wk ; Wv]^T ([B, T3, 2*Hkv*128] bf16; token t uses row
+    min(t, T3 - 1)); logits then hold 3 levels. Returns (k_out, v_out, lam
+    [B, T, L] fp32 or None).
     """
-    _check_cuda(y, logits, ema_state, ema_out)
-    _check_bf16(y)
+    _check_cuda(y, logits, ema_state, ema_out, y3)
+    _check_bf16(y, y3)
+    L = 3 if y3 is not None else 2
+    y3_sb = y3_st = 0
+    T3 = 0
+    if y3 is not None:
+        if y3.dim() != 3 or y3.shape[0] != B or y3.shape[2] != 2 * num_kv_heads * HEAD_DIM or y3.stride(2) != 1:
+            raise RuntimeError("route_ema_blend_kv: y3 must be [B, T3, 2*Hkv*128] with contiguous rows")
+        T3 = y3.shape[1]
+        y3_sb, y3_st = y3.stride(0), (y3.stride(1) if T3 > 1 else 0)
     N = 2 * num_kv_heads * HEAD_DIM
     if y.dim() != 2 or y.shape[0] != B * T or y.shape[1] != N or y.stride(1) != 1:
         raise RuntimeError(f"route_ema_blend_kv: y must be [B*T, {N}] with contiguous rows")
@@ -270,12 +280,12 @@ def route_ema_blend_kv(y: torch.Tensor, beta: float, logits: torch.Tensor, b2: O
         v_out = torch.empty_like(k_out)
     if k_out.stride() != v_out.stride():
         raise RuntimeError("route_ema_blend_kv: k and v outputs must share strides")
-    lam = torch.empty((B, T, 2), dtype=torch.float32, device=y.device) if want_lam else None
+    lam = torch.empty((B, T, L), dtype=torch.float32, device=y.device) if want_lam else None
     cos, sin, rsb, rst = _rope_args(rope, B, T)
     ws_bytes = _lib.load().fmka_route_ema_blend_kv_workspace_size(B, T, num_kv_heads)
     ws = _WS.get(y.device, ws_bytes)
     _lib.call("fmka_route_ema_blend_kv", y.data_ptr(), T * y.stride(0), y.stride(0), _ptr(logits.contiguous()),
-              _ptr(_f32(b2)), float(beta), B, T, num_kv_heads, _ptr(_f32(bias)), k_out.data_ptr(), v_out.data_ptr(),
+              _ptr(_f32(b2)), _ptr(y3), y3_sb, y3_st, T3, float(beta), B, T, num_kv_heads, _ptr(_f32(bias)), k_out.data_ptr(), v_out.data_ptr(),
               k_out.stride(0), k_out.stride(1), k_out.stride(2), t_offset, _ptr(cos), _ptr(sin), rsb, rst,
               _ptr(lam), _ptr(ema_state), _ptr(ema_out), _ptr(ws), ws_bytes, _stream(y))
     return k_out, v_out, lam

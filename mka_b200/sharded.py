@@ -24,7 +24,7 @@ import torch
 import torch.nn as nn
 
 from . import ops
-from .layers.forward import fastmka_forward
+from .layers.forward import fastmka_forward, project_l3
 from .layers.prepared import PreparedWeights
 
 HEAD_DIM = ops.HEAD_DIM
@@ -148,12 +148,11 @@ def fastmka_forward_heads(x: torch.Tensor, W: PreparedWeights, hq: int, hkv: int
     xb = xb.contiguous()
     L = 3 if use_l3 else 2
     q, logits = ops.qr_proj(xb.view(B * T, D), W.w_qr, W.b_qr, B, T, hq, W.router_hidden, W.w2, L, W.act, rope=rope)
-    l3 = None
-    if use_l3:
-        l3 = (torch.zeros((B, 1, D), dtype=torch.bfloat16, device=x.device) if l3_memory is None
-              else l3_memory.to(torch.bfloat16))
-    h, _ = ops.route_ema_blend(xb, beta, logits=logits, b2=W.b2, levels=L, l3=l3, want_lam=False)
-    k, v = ops.kv_proj(h.view(B * T, D), W.w_kv, W.b_kv, B, T, hkv, rope=rope)
+    # this rank's K/V only: the projection first, then the gate / EMA / blend
+    # scan over this rank's 2*hkv*128 channels (no stage replicated over d_model)
+    y = ops.gemm(xb.view(B * T, D), W.w_kv)
+    y3 = project_l3(l3_memory, W, B, D, hkv, x.device) if use_l3 else None
+    k, v, _ = ops.route_ema_blend_kv(y, beta, logits, W.b2, B, T, hkv, bias=W.b_kv, rope=rope, want_lam=False, y3=y3)
     o, _ = ops.attn_prefill(q, k, v, causal=True, want_lse=False)
     return o
 
