@@ -496,7 +496,8 @@ def run_kernel_only(args):
     g = torch.Generator(device=dev).manual_seed(0)
     c, d = PREFILL, DECODE
     n = args.warmup + args.steps
-    if args.only in ("attn_prefill", "route_ema_blend", "qr_proj", "kv_proj", "o_proj"):
+    if args.only in ("attn_prefill", "route_ema_blend", "route_ema_blend_h", "qr_proj", "kv_gemm", "kv_proj",
+                     "o_proj"):
         B = args.batch or c["B"]
         T, D = c["T"], c["D"]
         if args.only == "attn_prefill":
@@ -504,7 +505,7 @@ def run_kernel_only(args):
             k = torch.randn(B, c["HKV"], T, 128, generator=g, device=dev, dtype=torch.bfloat16)
             v = torch.randn(B, c["HKV"], T, 128, generator=g, device=dev, dtype=torch.bfloat16)
             fn = lambda: ops.attn_prefill(q, k, v)  # noqa: E731
-        elif args.only == "route_ema_blend":
+        elif args.only == "route_ema_blend_h":  # the blend-first stage 1 over d_model (op API)
             x = torch.randn(B, T, D, generator=g, device=dev, dtype=torch.bfloat16)
             lg = torch.randn(B * T, c["L"], generator=g, device=dev)
             fn = lambda: ops.route_ema_blend(x, 0.9, logits=lg, b2=None, levels=c["L"])  # noqa: E731
@@ -513,10 +514,17 @@ def run_kernel_only(args):
             W = layer.prepared(dev)
             x = (torch.randn(B * T, D, generator=g, device=dev) / math.sqrt(D)).to(torch.bfloat16)
             cos, sin = layer.rotary_emb.cos_sin(torch.arange(T, device=dev), dev)
-            if args.only == "qr_proj":
+            if args.only == "route_ema_blend":  # the layer's stage 1: on y = x [Wk ; Wv]^T, K/V out
+                y = (torch.randn(B * T, 2 * c["HKV"] * 128, generator=g, device=dev) * 0.05).to(torch.bfloat16)
+                lg = torch.randn(B * T, c["L"], generator=g, device=dev)
+                fn = lambda: ops.route_ema_blend_kv(y, 0.9, lg, W.b2, B, T, c["HKV"], bias=W.b_kv,  # noqa: E731
+                                                    rope=(cos, sin))
+            elif args.only == "kv_gemm":  # the layer's K/V GEMM: y = x [Wk ; Wv]^T
+                fn = lambda: ops.gemm(x, W.w_kv)  # noqa: E731
+            elif args.only == "qr_proj":
                 fn = lambda: ops.qr_proj(x, W.w_qr, W.b_qr, B, T, c["H"], W.router_hidden, W.w2, c["L"], W.act,  # noqa
                                          rope=(cos, sin))
-            elif args.only == "kv_proj":
+            elif args.only == "kv_proj":  # the blend-first K/V projection (op API)
                 fn = lambda: ops.kv_proj(x, W.w_kv, W.b_kv, B, T, c["HKV"], rope=(cos, sin))  # noqa: E731
             else:
                 fn = lambda: ops.gemm(x, W.w_o, W.b_o)  # noqa: E731
@@ -623,7 +631,8 @@ def main():
     ap.add_argument("--no-model", action="store_true",
                     help="skip the full Llama-3-8B model measurement (one GPU only)")
     ap.add_argument("--only", default=None,
-                    help="run one kernel alone (attn_prefill, attn_decode, route_ema_blend, qr_proj, kv_proj, o_proj)")
+                    help="run one kernel alone (attn_prefill, attn_decode, route_ema_blend, route_ema_blend_h, "
+                         "qr_proj, kv_gemm, kv_proj, o_proj)")
     ap.add_argument("--batch", type=int, default=0, help="batch override for --only")
     args = ap.parse_args()
     if args.only:
