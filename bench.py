@@ -360,14 +360,16 @@ def bench_decode(args, dist, rank, world, device, peaks):
 def bench_long_context(args, dist, rank, world, device, peaks):
     """The Qwen-7B-like layer with L3 retrieved memory at batch 2, seq 32768 (fixed
     total work): whole sequences per rank up to 2 GPUs, then kv heads split inside
-    each sequence's group with one NCCL all-gather before o_proj."""
+    each sequence's group; the group exchanges attention rows and o_proj rows by
+    the kernels' own stores into peer memory (`--exchange nccl`: an NCCL
+    all-gather before a replicated o_proj)."""
     from mka_b200.sharded import HeadShardedFastMKA, make_groups
 
     c = LONG
     B, T, D = c["B"], c["T"], c["D"]
     layer = build_layer(c, device, seed=2)
     groups = make_groups(B, c["HKV"], world) if dist is not None else {}
-    sh = HeadShardedFastMKA(layer, B, rank, world, groups)
+    sh = HeadShardedFastMKA(layer, B, rank, world, groups, transport=args.exchange)
     b0, b1 = sh.plan.batch
     g = torch.Generator(device=device).manual_seed(3000)
     x = (torch.randn(B, T, D, generator=g, device=device) / math.sqrt(D)).to(torch.bfloat16)[b0:b1].contiguous()
@@ -401,11 +403,15 @@ def bench_long_context(args, dist, rank, world, device, peaks):
     attn_ms = a.elapsed_time(e) / steps
     flops = 4.0 * (b1 - b0) * hq * 128 * T * (T + 1) / 2
     achieved = flops / (attn_ms * 1e-3) / 1e12
+    gsz = len(sh.plan.group)
+    sh.close()
+    exchange = ("none" if gsz == 1 else "peer stores from the attention and o_proj epilogues"
+                if args.exchange == "peer" else "NCCL all-gather, o_proj on every rank")
     return {"metric": "FastMKA prefill tokens/s, long context with L3 (fixed total work)",
             "value": B * T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "scaling": "strong",
             "config": {"batch": B, "seq_len": T, "d_model": D, "heads": f"{c['H']}/{c['HKV']}", "levels": 3,
                        "router": f"{D}->{c['R']}->3", "partition": f"sequences x kv heads, group size "
-                                                                  f"{len(sh.plan.group)}"},
+                                                                  f"{gsz}", "exchange": exchange},
             "roofline": {"bound": "tensor", "kernel": "attn_prefill (this rank's heads, T=32768)",
                          "achieved": round(achieved, 1), "peak": peaks["bf16"], "unit": "TFLOP/s",
                          "frac": round(achieved / peaks["bf16"], 4), "peak_kind": f"{peaks['src']} burst bf16",
@@ -628,6 +634,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-long", action="store_true", help="skip the long-context (L3, seq 32768) measurement")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="how a head-sharded sequence group exchanges rows (long context, N > 2)")
     ap.add_argument("--no-model", action="store_true",
                     help="skip the full Llama-3-8B model measurement (one GPU only)")
     ap.add_argument("--only", default=None,

@@ -6,7 +6,7 @@
  * fmka_get_last_error() returns the message of the calling thread's last error.
  * The caller owns every buffer; scratch memory ("workspace") is passed in by the
  * caller with its size, and each *_workspace_size() function reports how much a
- * call needs. No entry point allocates device memory; kernels report bounded-
+ * call needs. No entry point but fmka_peer_alloc allocates device memory; kernels report bounded-
  * wait timeouts through a status word that lives in the library's own device
  * data. Calls on distinct streams with distinct buffers may run concurrently.
  *
@@ -38,6 +38,12 @@
  *                           (fastmka.py:175-176; hf/attention.py:194-195)
  *   fmka_get_last_error     the TORCH_CHECK / cudaGetLastError error reporting of
  *                           fastmka_attn.cu:134-150,169-170
+ *   fmka_attn_fwd_prefill_scatter, fmka_gemm_bf16_kblocked_scatter, fmka_peer_*
+ *                           the head-sharded layer over several GPUs of a box:
+ *                           attention rows and o_proj rows stored straight into
+ *                           the other ranks' buffers, which replaces an all-gather
+ *                           in front of o_proj (the reference keeps distributed
+ *                           code in scripts/train_hf_patch.py:97-129)
  */
 #ifndef FASTMKA_B200_H_
 #define FASTMKA_B200_H_
@@ -70,7 +76,8 @@ enum {
 enum {
   FMKA_STATUS_WAIT_TIMEOUT = 1,     /* a pipeline wait in a kernel ran out of time */
   FMKA_STATUS_LOOKBACK_TIMEOUT = 2, /* the EMA scan's look-back ran out of time */
-  FMKA_STATUS_BAD_LAUNCH = 4
+  FMKA_STATUS_BAD_LAUNCH = 4,
+  FMKA_STATUS_PEER_TIMEOUT = 8      /* a cross-GPU barrier (fmka_peer_barrier) ran out of time */
 };
 
 /* Library version string. */
@@ -225,6 +232,46 @@ FMKA_API int fmka_attn_decode_splitkv(const void* q, int64_t q_sb, int64_t q_sh,
                              int64_t kv_sh, int64_t kv_st, void* o, int64_t o_sb, int64_t o_sh, float* lse,
                              int64_t lse_sb, int B, int Hq, int Hkv, int Tk, int head_dim, float scale,
                              int num_splits, void* workspace, size_t workspace_bytes, fmka_stream_t stream);
+
+/* ------------------------------------------------ several GPUs of a box ---
+ * The ranks of a sequence group (one process per GPU) share buffers through
+ * peer mappings: fmka_peer_alloc makes a zero-filled device allocation (the one
+ * entry point that allocates: a mapping covers a whole allocation), whose
+ * FMKA_PEER_HANDLE_BYTES-byte handle from fmka_peer_export another process of
+ * the box opens with fmka_peer_import (close it with fmka_peer_close before the
+ * owner calls fmka_peer_free). No multicast object is created.
+ *
+ * fmka_peer_barrier: flags[j] is rank j's array of n uint32 slots as mapped in
+ * the calling process (its own array for j == rank). In stream order, the
+ * caller stores `epoch` into slot `rank` of every array and waits until every
+ * slot of its own array holds `epoch` or later; epochs must grow by one per
+ * barrier, starting from 1 on zero-filled arrays. A wait that runs out of time
+ * (2 s) sets FMKA_STATUS_PEER_TIMEOUT and returns. */
+#define FMKA_PEER_HANDLE_BYTES 64
+FMKA_API int fmka_peer_alloc(size_t bytes, void** ptr);
+FMKA_API int fmka_peer_free(void* ptr);
+FMKA_API int fmka_peer_export(const void* ptr, void* handle);
+FMKA_API int fmka_peer_import(const void* handle, void** ptr);
+FMKA_API int fmka_peer_close(void* ptr);
+FMKA_API int fmka_peer_barrier(uint32_t* const* flags, int rank, int n, uint32_t epoch, fmka_stream_t stream);
+
+/* fmka_attn_fwd_prefill with the output rows split over n_dst (<= 8) buffers:
+ * query rows [j * rows_per_dst, (j + 1) * rows_per_dst) of every sequence go to
+ * o_dst[j] (row t - j * rows_per_dst there, strides o_sb / o_st / o_sh), local
+ * or peer-mapped. No LSE. n_dst * rows_per_dst must cover Tq. */
+FMKA_API int fmka_attn_fwd_prefill_scatter(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, const void* k,
+                                  const void* v, int64_t kv_sb, int64_t kv_sh, int64_t kv_st, void* const* o_dst,
+                                  int n_dst, int rows_per_dst, int64_t o_sb, int64_t o_st, int64_t o_sh, int B,
+                                  int Hq, int Hkv, int Tq, int Tk, int head_dim, int causal, float scale,
+                                  fmka_stream_t stream);
+
+/* fmka_gemm_bf16_kblocked whose output row m is written to row c_row0 + m of
+ * each of the n_dst (<= 8) buffers c_dst[0 .. n_dst-1] (row stride ldc), local
+ * or peer-mapped: o_proj on this rank's rows, delivered to every rank of the
+ * group. N and ldc must be multiples of 8, the buffers 16-byte aligned. */
+FMKA_API int fmka_gemm_bf16_kblocked_scatter(const void* a, int a_kblk, int64_t a_blk_stride, int64_t lda,
+                                    const void* w, int64_t ldw, const float* bias, void* const* c_dst, int n_dst,
+                                    int64_t c_row0, int64_t ldc, int M, int N, int K, fmka_stream_t stream);
 
 #ifdef __cplusplus
 }

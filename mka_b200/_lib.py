@@ -44,6 +44,15 @@ _SIGNATURES = {
     "fmka_route_blend": (_I, [_P, _L, _L, _P, _L, _L, _P, _L, _L, _I, _P, _I, _I, _I, _I, _P, _L, _L, _P]),
     "fmka_attn_fwd_prefill": (_I, [_P, _L, _L, _L, _P, _P, _L, _L, _L, _P, _L, _L, _L, _P, _L, _L,
                                    _I, _I, _I, _I, _I, _I, _I, _F, _P]),
+    "fmka_attn_fwd_prefill_scatter": (_I, [_P, _L, _L, _L, _P, _P, _L, _L, _L, _P, _I, _I, _L, _L, _L,
+                                           _I, _I, _I, _I, _I, _I, _I, _F, _P]),
+    "fmka_gemm_bf16_kblocked_scatter": (_I, [_P, _I, _L, _L, _P, _L, _P, _P, _I, _L, _L, _I, _I, _I, _P]),
+    "fmka_peer_alloc": (_I, [c_size_t, POINTER(_P)]),
+    "fmka_peer_free": (_I, [_P]),
+    "fmka_peer_export": (_I, [_P, _P]),
+    "fmka_peer_import": (_I, [_P, POINTER(_P)]),
+    "fmka_peer_close": (_I, [_P]),
+    "fmka_peer_barrier": (_I, [_P, _I, _I, c_uint32, _P]),
     "fmka_attn_decode_num_splits": (_I, [_I, _I, _I]),
     "fmka_attn_decode_workspace_size": (c_size_t, [_I, _I, _I, _I, _I]),
     "fmka_attn_decode_splitkv": (_I, [_P, _L, _L, _P, _P, _L, _L, _L, _P, _L, _L, _P, _L,

@@ -78,6 +78,11 @@ struct AttnParams {
   float scale_log2;  // softmax scale * log2(e)
   __nv_bfloat16* o;  // O[b, t, h, :]
   int64_t o_sb, o_st, o_sh;
+  // o_rows_per_dst > 0: query rows [j * o_rows_per_dst, (j + 1) * o_rows_per_dst)
+  // of every sequence go to o_dst.p[j] (row t - j * o_rows_per_dst there), a
+  // local or peer-mapped buffer with the same strides; p.o is unused.
+  int o_rows_per_dst;
+  PeerPtrs o_dst;
   float* lse;        // lse[b, h, t] (may be null)
   int64_t lse_sb, lse_sh;
   int n_qblocks;
@@ -419,7 +424,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const float inv = z > 0.f ? 1.f / z : 0.f;
         const bool row_ok = q < p.Tq;
-        __nv_bfloat16* dst = p.o + (int64_t)b * p.o_sb + (int64_t)q * p.o_st + (int64_t)hq * p.o_sh;
+        __nv_bfloat16* obase = p.o;
+        int qo = q;
+        if (p.o_rows_per_dst > 0 && row_ok) {
+          const int j = q / p.o_rows_per_dst;
+          obase = p.o_dst.p[j];
+          qo = q - j * p.o_rows_per_dst;
+        }
+        __nv_bfloat16* dst = obase + (int64_t)b * p.o_sb + (int64_t)qo * p.o_st + (int64_t)hq * p.o_sh;
 #pragma unroll 1
         for (int c4 = 0; c4 < 4; ++c4) {
           uint32_t o[32];
@@ -441,6 +453,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row_ok && p.lse != nullptr) {
           p.lse[(int64_t)b * p.lse_sb + (int64_t)hq * p.lse_sh + q] = m_used * 0.69314718055994531f + __logf(z);
         }
+        // Rows stored into peer memory are ordered before whatever this GPU
+        // does next (the barrier kernel that announces them to the peers).
+        if (p.o_rows_per_dst > 0) __threadfence_system();
       } else {
         *abort_flag = 1;
       }
@@ -462,9 +477,19 @@ int launch_attn_prefill(const __nv_bfloat16* q, int64_t q_sb, int64_t q_sh, int6
                         const __nv_bfloat16* k, const __nv_bfloat16* v, int64_t kv_sb, int64_t kv_sh,
                         int64_t kv_st, __nv_bfloat16* o, int64_t o_sb, int64_t o_st, int64_t o_sh, float* lse,
                         int64_t lse_sb, int64_t lse_sh, int B, int Hq, int Hkv, int Tq, int Tk, int head_dim,
-                        int causal, float scale, cudaStream_t stream) {
+                        int causal, float scale, cudaStream_t stream, const PeerPtrs* o_dst, int n_dst,
+                        int rows_per_dst) {
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Tq <= 0 || Tk <= 0)
     return set_error(kErrInvalidArgument, "attn_prefill: empty shape");
+  const bool scatter = o_dst != nullptr;
+  if (scatter) {
+    if (n_dst < 1 || n_dst > kMaxPeers || rows_per_dst <= 0 || (int64_t)rows_per_dst * n_dst < Tq)
+      return set_error(kErrInvalidArgument, "attn_prefill: scatter destinations do not cover the query rows");
+    for (int j = 0; j < n_dst; ++j)
+      if (o_dst->p[j] == nullptr || (reinterpret_cast<uintptr_t>(o_dst->p[j]) & 15u))
+        return set_error(kErrInvalidArgument, "attn_prefill: scatter destinations must be 16-byte aligned");
+    o = o_dst->p[0];
+  }
   if (head_dim != kHeadDim) return set_error(kErrUnsupported, "attn_prefill: head_dim must be 128");
   if (Hq % Hkv != 0) return set_error(kErrInvalidArgument, "attn_prefill: query heads must be a multiple of kv heads");
   if (causal && Tk < Tq) return set_error(kErrInvalidArgument, "attn_prefill: causal attention needs Tk >= Tq");
@@ -503,6 +528,8 @@ int launch_attn_prefill(const __nv_bfloat16* q, int64_t q_sb, int64_t q_sh, int6
   p.o_sb = o_sb;
   p.o_st = o_st;
   p.o_sh = o_sh;
+  p.o_rows_per_dst = scatter ? rows_per_dst : 0;
+  for (int j = 0; j < kMaxPeers; ++j) p.o_dst.p[j] = (scatter && j < n_dst) ? o_dst->p[j] : nullptr;
   p.lse = lse;
   p.lse_sb = lse_sb;
   p.lse_sh = lse_sh;

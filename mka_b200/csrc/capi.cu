@@ -40,7 +40,9 @@ int launch_attn_prefill(const __nv_bfloat16* q, int64_t q_sb, int64_t q_sh, int6
                         const __nv_bfloat16* k, const __nv_bfloat16* v, int64_t kv_sb, int64_t kv_sh,
                         int64_t kv_st, __nv_bfloat16* o, int64_t o_sb, int64_t o_st, int64_t o_sh, float* lse,
                         int64_t lse_sb, int64_t lse_sh, int B, int Hq, int Hkv, int Tq, int Tk, int head_dim,
-                        int causal, float scale, cudaStream_t stream);
+                        int causal, float scale, cudaStream_t stream, const PeerPtrs* o_dst = nullptr,
+                        int n_dst = 0, int rows_per_dst = 0);
+int launch_peer_barrier(uint32_t* const* flags, int rank, int n, uint32_t epoch, cudaStream_t stream);
 size_t attn_decode_workspace_bytes(int B, int Hq, int num_splits);
 int attn_decode_plan(int B, int Hkv, int Tk, int requested, int* keys_per_split_out);
 int launch_attn_decode(const __nv_bfloat16* q, int64_t q_sb, int64_t q_sh, const __nv_bfloat16* k,
@@ -417,6 +419,100 @@ int fmka_attn_fwd_prefill(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_s
     return set_error(kErrInvalidArgument, "attn_prefill: null pointer");
   return launch_attn_prefill(bf(q), q_sb, q_sh, q_st, bf(k), bf(v), kv_sb, kv_sh, kv_st, bfw(o), o_sb, o_st, o_sh,
                              lse, lse_sb, lse_sh, B, Hq, Hkv, Tq, Tk, head_dim, causal, scale, as_stream(stream));
+}
+
+int fmka_attn_fwd_prefill_scatter(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, const void* k,
+                                  const void* v, int64_t kv_sb, int64_t kv_sh, int64_t kv_st, void* const* o_dst,
+                                  int n_dst, int rows_per_dst, int64_t o_sb, int64_t o_st, int64_t o_sh, int B,
+                                  int Hq, int Hkv, int Tq, int Tk, int head_dim, int causal, float scale,
+                                  fmka_stream_t stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || o_dst == nullptr)
+    return set_error(kErrInvalidArgument, "attn_prefill_scatter: null pointer");
+  if (n_dst < 1 || n_dst > kMaxPeers)
+    return set_error(kErrInvalidArgument, "attn_prefill_scatter: 1 to 8 destinations");
+  PeerPtrs d;
+  for (int j = 0; j < kMaxPeers; ++j) d.p[j] = j < n_dst ? static_cast<__nv_bfloat16*>(o_dst[j]) : nullptr;
+  return launch_attn_prefill(bf(q), q_sb, q_sh, q_st, bf(k), bf(v), kv_sb, kv_sh, kv_st, d.p[0], o_sb, o_st, o_sh,
+                             nullptr, 0, 0, B, Hq, Hkv, Tq, Tk, head_dim, causal, scale, as_stream(stream), &d, n_dst,
+                             rows_per_dst);
+}
+
+int fmka_gemm_bf16_kblocked_scatter(const void* a, int a_kblk, int64_t a_blk_stride, int64_t lda, const void* w,
+                                    int64_t ldw, const float* bias, void* const* c_dst, int n_dst, int64_t c_row0,
+                                    int64_t ldc, int M, int N, int K, fmka_stream_t stream) {
+  if (a == nullptr || w == nullptr || c_dst == nullptr) return set_error(kErrInvalidArgument, "gemm: null pointer");
+  if (a_kblk <= 0) return set_error(kErrInvalidArgument, "gemm: a_kblk must be positive");
+  if (n_dst < 1 || n_dst > kMaxPeers) return set_error(kErrInvalidArgument, "gemm: 1 to 8 scatter destinations");
+  if (bias != nullptr && !al16(bias)) return set_error(kErrInvalidArgument, "gemm: bias must be 16-byte aligned");
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.a_kblk = a_kblk;
+  p.a_blk_stride = a_blk_stride;
+  p.n_split = N;
+  p.seg[0] = empty_seg();
+  p.seg[0].kind = kSegRowMajor;
+  p.seg[0].n_begin = 0;
+  p.seg[0].n_end = N;
+  p.seg[0].bias = bias;
+  p.seg[1] = empty_seg();
+  p.status = device_status_word();
+  p.n_dst = n_dst;
+  p.dst_row0 = c_row0;
+  p.dst_ld = ldc;
+  for (int j = 0; j < kMaxPeers; ++j) p.dst.p[j] = j < n_dst ? static_cast<__nv_bfloat16*>(c_dst[j]) : nullptr;
+  return launch_gemm(bf(a), lda, bf(w), ldw, p, num_sms_current_device(), as_stream(stream));
+}
+
+int fmka_peer_alloc(size_t bytes, void** ptr) {
+  if (ptr == nullptr || bytes == 0) return set_error(kErrInvalidArgument, "peer_alloc: null pointer or zero size");
+  *ptr = nullptr;
+  void* p = nullptr;
+  int rc = check_cuda(cudaMalloc(&p, bytes), "peer_alloc");
+  if (rc) return rc;
+  rc = check_cuda(cudaMemset(p, 0, bytes), "peer_alloc zero");
+  if (rc) {
+    cudaFree(p);
+    return rc;
+  }
+  *ptr = p;
+  return kOk;
+}
+
+int fmka_peer_free(void* ptr) {
+  if (ptr == nullptr) return kOk;
+  return check_cuda(cudaFree(ptr), "peer_free");
+}
+
+static_assert(sizeof(cudaIpcMemHandle_t) == FMKA_PEER_HANDLE_BYTES, "IPC handle size");
+
+int fmka_peer_export(const void* ptr, void* handle) {
+  if (ptr == nullptr || handle == nullptr) return set_error(kErrInvalidArgument, "peer_export: null pointer");
+  cudaIpcMemHandle_t h;
+  int rc = check_cuda(cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)), "peer_export");
+  if (rc) return rc;
+  std::memcpy(handle, &h, sizeof(h));
+  return kOk;
+}
+
+int fmka_peer_import(const void* handle, void** ptr) {
+  if (ptr == nullptr || handle == nullptr) return set_error(kErrInvalidArgument, "peer_import: null pointer");
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return check_cuda(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "peer_import");
+}
+
+int fmka_peer_close(void* ptr) {
+  if (ptr == nullptr) return kOk;
+  return check_cuda(cudaIpcCloseMemHandle(ptr), "peer_close");
+}
+
+int fmka_peer_barrier(uint32_t* const* flags, int rank, int n, uint32_t epoch, fmka_stream_t stream) {
+  if (flags == nullptr) return set_error(kErrInvalidArgument, "peer_barrier: null pointer");
+  return launch_peer_barrier(flags, rank, n, epoch, as_stream(stream));
 }
 
 int fmka_attn_decode_num_splits(int B, int Hkv, int Tk) {

@@ -34,6 +34,15 @@ int check_cuda(cudaError_t e, const char* what);
 int make_tmap_bf16(CUtensorMap* out, const void* base, int rank, const uint64_t* dims,
                    const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128);
 
+// ------------------------------------------------------------ peer memory --
+// Most ranks (GPUs of one box) that exchange data through peer mappings.
+constexpr int kMaxPeers = 8;
+
+// Pointers into the same buffer as mapped in each rank (index = rank in group).
+struct PeerPtrs {
+  __nv_bfloat16* p[kMaxPeers];
+};
+
 // ------------------------------------------------------------------- GEMM --
 enum SegKind : int { kSegRowMajor = 0, kSegHeads = 1, kSegRouter = 2 };
 
@@ -64,6 +73,13 @@ struct GemmParams {
   int n_split;  // columns < n_split use seg[0], the rest seg[1]
   GemmSeg seg[2];
   uint32_t* status;
+  // Scatter epilogue (n_dst > 0, replaces the segments): bias seg[0].bias,
+  // output row m written to row dst_row0 + m of every dst.p[0 .. n_dst-1]
+  // (row stride dst_ld), each a local or a peer-mapped [*, N] bf16 buffer.
+  int n_dst;
+  int64_t dst_row0;
+  int64_t dst_ld;
+  PeerPtrs dst;
 };
 
 // C = A[M,K] * B[N,K]^T with the segment epilogues. A and B are row-major bf16

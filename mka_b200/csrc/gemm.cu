@@ -235,6 +235,77 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams& p, int m, b
   }
 }
 
+// Scatter epilogue (p.n_dst > 0) of one accumulator tile for the calling warp's
+// 32 rows m_warp0 .. m_warp0 + 31: bias, bf16, and a store of every row into
+// each destination buffer (mostly other GPUs' memory through peer mappings).
+// The rows pass through the warp's 8 KB staging area in shared memory (32 rows
+// x 128 columns, 16-byte units XOR-swizzled by row so that neither side has
+// bank conflicts), so that every store instruction writes two whole 256-byte
+// row segments instead of 32 scattered 16-byte pieces: full-width writes keep
+// the NVLink packets full.
+constexpr int kScatterWarpBytes = 32 * 128 * 2;
+
+template <int BN>
+__device__ __forceinline__ void gemm_epilogue_scatter(const GemmParams& p, int m_warp0, int n0, uint32_t acc_addr,
+                                                      uint4* stage) {
+  const int lane = lane_id();
+  const float* bias = p.seg[0].bias;
+#pragma unroll 1
+  for (int h = 0; h < BN / 128; ++h) {
+    const int nh = n0 + h * 128;
+    if (nh >= p.N) break;  // warp-uniform
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t r[32];
+      tmem_ld32(acc_addr + h * 128 + c * 32, r);
+      tmem_wait_ld();
+      const int n = nh + c * 32;
+      if (bias != nullptr) {
+        if (n + 32 <= p.N) {
+          const float4* b4 = reinterpret_cast<const float4*>(bias + n);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 bb = __ldg(b4 + q);
+            r[4 * q + 0] = __float_as_uint(__uint_as_float(r[4 * q + 0]) + bb.x);
+            r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + bb.y);
+            r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + bb.z);
+            r[4 * q + 3] = __float_as_uint(__uint_as_float(r[4 * q + 3]) + bb.w);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n + j < p.N) r[j] = __float_as_uint(__uint_as_float(r[j]) + __ldg(bias + n + j));
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        w.x = pack_bf16x2(__uint_as_float(r[q * 8 + 0]), __uint_as_float(r[q * 8 + 1]));
+        w.y = pack_bf16x2(__uint_as_float(r[q * 8 + 2]), __uint_as_float(r[q * 8 + 3]));
+        w.z = pack_bf16x2(__uint_as_float(r[q * 8 + 4]), __uint_as_float(r[q * 8 + 5]));
+        w.w = pack_bf16x2(__uint_as_float(r[q * 8 + 6]), __uint_as_float(r[q * 8 + 7]));
+        stage[lane * 16 + ((c * 4 + q) ^ (lane & 7))] = w;
+      }
+    }
+    __syncwarp();
+    // Lanes 0-15 store row 2i, lanes 16-31 row 2i + 1, 16 bytes each.
+    const int u = lane & 15;
+    const bool col_ok = nh + u * 8 < p.N;  // N is a multiple of 8
+#pragma unroll 4
+    for (int i = 0; i < 16; ++i) {
+      const int rr = 2 * i + (lane >> 4);
+      const int m = m_warp0 + rr;
+      const uint4 w = stage[rr * 16 + (u ^ (rr & 7))];
+      if (m < p.M && col_ok) {
+        const int64_t off = (p.dst_row0 + m) * p.dst_ld + nh + u * 8;
+#pragma unroll 1
+        for (int k = 0; k < p.n_dst; ++k) *reinterpret_cast<uint4*>(p.dst.p[k] + off) = w;
+      }
+    }
+    __syncwarp();  // the staging area is read before the next half overwrites it
+  }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -429,8 +500,12 @@ struct PairCfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * kBN;
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+  // With the scatter epilogue: plus the four epilogue warps' staging areas.
+  static constexpr int kScatterBytes = 4 * kScatterWarpBytes;
+  static constexpr int kSmemBytesScatter = kSmemBytes + kScatterBytes;
 };
 
+template <bool kScatter>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ GemmParams p) {
@@ -442,7 +517,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + S * Cfg::kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint4* sScatter = reinterpret_cast<uint4*>(smem + S * Cfg::kStageBytes);
+  uint64_t* bars =
+      reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes + (kScatter ? Cfg::kScatterBytes : 0));
   uint64_t* full = bars;               // [S]  used in the even CTA
   uint64_t* empty = bars + S;          // [S]  both CTAs
   uint64_t* tfull = bars + 2 * S;      // [2]  both CTAs
@@ -591,11 +668,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int m = (tile / num_n) * (2 * kBM) + (int)rank * kBM + row_in_tile;
       const int n0 = (tile % num_n) * BN;
-      gemm_epilogue_tile<BN>(p, m, m < p.M, n0, lane_addr + acc * BN);
+      if constexpr (kScatter)
+        gemm_epilogue_scatter<BN>(p, m - lane, n0, lane_addr + acc * BN,
+                                  sScatter + ew * (kScatterWarpBytes / 16));
+      else
+        gemm_epilogue_tile<BN>(p, m, m < p.M, n0, lane_addr + acc * BN);
       tc_fence_before();
       __syncwarp();  // every lane's TMEM reads have completed before the warp's arrival
       if (lane == 0) mbar_arrive_cluster(tempty_even + acc * 8);
     }
+    // Stores into peer memory are ordered before whatever this GPU does next
+    // (the barrier kernel that announces them to the peers).
+    if constexpr (kScatter) __threadfence_system();
   }
 
   __syncwarp();
@@ -835,6 +919,18 @@ int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int
   if (p.M <= kBM) BN = 128;
   if (p.n_split % 128 != 0 && p.n_split < p.N)
     return set_error(kErrInvalidArgument, "gemm: segment split must be a multiple of 128 columns");
+  // Scatter epilogue: always the CTA-pair kernel with 256-wide tiles.
+  const bool scatter = p.n_dst > 0;
+  if (scatter) {
+    if (p.n_dst > kMaxPeers) return set_error(kErrInvalidArgument, "gemm: at most 8 scatter destinations");
+    if (p.N % 8 != 0 || p.dst_ld % 8 != 0 || p.dst_ld < p.N || p.dst_row0 < 0 || p.n_split < p.N)
+      return set_error(kErrInvalidArgument, "gemm: scatter needs N and the row stride multiples of 8, one segment");
+    for (int k = 0; k < p.n_dst; ++k)
+      if (p.dst.p[k] == nullptr || (reinterpret_cast<uintptr_t>(p.dst.p[k]) & 15u))
+        return set_error(kErrInvalidArgument, "gemm: scatter destinations must be 16-byte aligned");
+    if (num_sms < 2) return set_error(kErrUnsupported, "gemm: scatter needs two SMs");
+    BN = 256;
+  }
   for (int s = 0; s < 2; ++s) {
     const GemmSeg& g = p.seg[s];
     if (g.n_end <= g.n_begin) continue;
@@ -870,7 +966,7 @@ int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int
     const char* e = std::getenv("FMKA_GEMM_PAIR");
     return e == nullptr || e[0] != '0';
   }();
-  const bool use_pair = pair_enabled && BN == 256 && p.M > kBM && num_sms >= 2;
+  const bool use_pair = scatter || (pair_enabled && BN == 256 && p.M > kBM && num_sms >= 2);
   {
     uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.N};
     uint64_t strides[1] = {(uint64_t)ldb * 2};
@@ -885,7 +981,7 @@ int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int
     const char* e = std::getenv("FMKA_GEMM_SPLITK");
     return e == nullptr || e[0] != '0';
   }();
-  if (splitk_enabled && BN == 128 && p.M <= kSplitRows) {
+  if (!scatter && splitk_enabled && BN == 128 && p.M <= kSplitRows) {
     const int tiles = (p.N + BN - 1) / BN;
     const int num_kb = (p.K + kBK - 1) / kBK;
     int cs = num_sms / tiles;
@@ -918,11 +1014,12 @@ int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int
   if (use_pair) {
     const int tiles = ((p.M + 2 * kBM - 1) / (2 * kBM)) * ((p.N + PairCfg::kBN - 1) / PairCfg::kBN);
     const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
-    const int smem = PairCfg::kSmemBytes;
-    int rc = check_cuda(cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+    const int smem = scatter ? PairCfg::kSmemBytesScatter : PairCfg::kSmemBytes;
+    auto kern = scatter ? gemm_pair_kernel<true> : gemm_pair_kernel<false>;
+    int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                         "gemm pair attr");
     if (rc) return rc;
-    gemm_pair_kernel<<<2 * pairs, kThreads, smem, stream>>>(tmA, tmB, p);
+    kern<<<2 * pairs, kThreads, smem, stream>>>(tmA, tmB, p);
     return check_cuda(cudaGetLastError(), "gemm pair launch");
   }
 

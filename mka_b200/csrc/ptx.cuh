@@ -23,6 +23,7 @@ enum : uint32_t {
   kStatusWaitTimeout = 1u << 0,    // an mbarrier / flag wait ran out of time
   kStatusLookbackTimeout = 1u << 1,  // the EMA scan's look-back ran out of time
   kStatusBadLaunch = 1u << 2,      // a kernel saw arguments it cannot handle
+  kStatusPeerTimeout = 1u << 3,    // a cross-GPU flag barrier ran out of time
 };
 
 // Wait budget: 2 s of wall-clock time per wait.

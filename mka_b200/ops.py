@@ -13,7 +13,7 @@ fused_route_mka_attn :47-70, has_fastmka_cuda :25-26, has_fused_route_mka_cuda
 from __future__ import annotations
 
 import math
-from typing import Optional, Tuple
+from typing import Optional, Sequence, Tuple
 
 import torch
 
@@ -117,6 +117,27 @@ def gemm_kblocked(a_blocks: torch.Tensor, w: torch.Tensor, bias: Optional[torch.
     _lib.call("fmka_gemm_bf16_kblocked", a_blocks.data_ptr(), kb, a_blocks.stride(0), a_blocks.stride(1),
               w.data_ptr(), w.stride(0), _ptr(b32), out.data_ptr(), out.stride(0), M, N, K, _stream(a_blocks))
     return out
+
+
+def gemm_kblocked_scatter(a_blocks: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
+                          dst_ptrs: Sequence[int], row0: int, ldc: int) -> None:
+    """gemm_kblocked whose output row m goes to row row0 + m of every buffer in
+    dst_ptrs (device addresses of bf16 [*, ldc] buffers, local or peer-mapped;
+    at most 8). Nothing is returned: the rows land in the destinations."""
+    _check_cuda(a_blocks, w)
+    _check_bf16(a_blocks, w)
+    if a_blocks.dim() != 3 or a_blocks.stride(2) != 1:
+        raise RuntimeError("gemm_kblocked_scatter: a_blocks must be [nblk, M, kb] with a contiguous last dimension")
+    nblk, M, kb = a_blocks.shape
+    K = nblk * kb
+    if w.shape[1] != K:
+        raise RuntimeError("gemm_kblocked_scatter: w must be [N, nblk * kb]")
+    N = w.shape[0]
+    n = len(dst_ptrs)
+    arr = (_lib.ctypes.c_void_p * max(n, 1))(*dst_ptrs)
+    b32 = _f32(bias)
+    _lib.call("fmka_gemm_bf16_kblocked_scatter", a_blocks.data_ptr(), kb, a_blocks.stride(0), a_blocks.stride(1),
+              w.data_ptr(), w.stride(0), _ptr(b32), arr, n, int(row0), int(ldc), M, N, K, _stream(a_blocks))
 
 
 def qr_proj(x2d: torch.Tensor, w_qr: torch.Tensor, bias_qr: Optional[torch.Tensor], B: int, T: int,
@@ -333,6 +354,29 @@ def attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool
               lse.stride(1) if lse is not None else 0, B, Hq, Hkv, Tq, Tk, Dh, int(causal), float(scale),
               _stream(q))
     return out, lse
+
+
+def attn_prefill_scatter(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dst_ptrs: Sequence[int],
+                         rows_per_dst: int, o_strides: Tuple[int, int, int], causal: bool = True,
+                         scale: Optional[float] = None) -> None:
+    """attn_prefill with the output rows split over several buffers: query rows
+    [j * rows_per_dst, (j + 1) * rows_per_dst) go to dst_ptrs[j] (device
+    addresses, local or peer-mapped; at most 8), indexed [b, t, h, :] with
+    element strides o_strides = (sb, st, sh). No LSE."""
+    _check_cuda(q, k, v)
+    _check_bf16(q, k, v)
+    B, Hq, Tq, Dh = q.shape
+    _, Hkv, Tk, _ = k.shape
+    if k.stride() != v.stride() or k.shape != v.shape:
+        raise RuntimeError("attn_prefill_scatter: k and v must have the same shape and strides")
+    if scale is None:
+        scale = 1.0 / math.sqrt(Dh)
+    n = len(dst_ptrs)
+    arr = (_lib.ctypes.c_void_p * max(n, 1))(*dst_ptrs)
+    sb, st, sh = o_strides
+    _lib.call("fmka_attn_fwd_prefill_scatter", q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), k.data_ptr(),
+              v.data_ptr(), k.stride(0), k.stride(1), k.stride(2), arr, n, int(rows_per_dst), int(sb), int(st),
+              int(sh), B, Hq, Hkv, Tq, Tk, Dh, int(causal), float(scale), _stream(q))
 
 
 def attn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Optional[float] = None,

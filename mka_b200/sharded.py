@@ -8,12 +8,23 @@ heads, and the fused memory of that sequence.
   * world <= batch: every rank owns whole sequences (batch / world of them)
     and runs the unsharded layer on them; no collective at all.
   * world > batch: the ranks of a sequence group (world / batch ranks per
-    sequence) split the kv heads. Each rank computes stage 1 (router gate, EMA
-    scan, blend) for its sequence - the router needs all of q, so its first
-    layer is not split - and Q, K, V and causal attention for its own heads.
-    One NCCL all-gather of the attention output inside the group feeds
-    o_proj, which reads the gathered [ranks, B*T, heads*128] buffer in place
-    (fmka_gemm_bf16_kblocked) and yields the full output on every rank.
+    sequence) split the kv heads. Each rank computes the router for its
+    sequence - it needs all of q, so its first layer is not split - and Q, K,
+    V (stage 1 in the projected space of its own kv heads) and causal
+    attention for its own heads. Then the group exchanges data in one of two
+    ways (`transport`):
+      "peer" (default): the sequence's T rows are split into one block per
+        rank. The attention kernel stores each row block of its output
+        straight into the owning rank's gather buffer (peer memory over
+        NVLink); after a flag barrier each rank runs o_proj on its own row
+        block only - a 1/gs share of the o_proj FLOPs - and the GEMM's
+        epilogue stores every output row into all ranks' output buffers;
+        a second barrier completes the step. Two kernels carry both
+        exchanges; no collective library call and no replicated o_proj.
+      "nccl": one NCCL all-gather of the attention output feeds o_proj,
+        which reads the gathered [ranks, B*T, heads*128] buffer in place
+        (fmka_gemm_bf16_kblocked) and runs whole on every rank.
+    Either way every rank ends with the full layer output of its sequence.
 """
 from __future__ import annotations
 
@@ -26,6 +37,7 @@ import torch.nn as nn
 from . import ops
 from .layers.forward import fastmka_forward, project_l3
 from .layers.prepared import PreparedWeights
+from .peer import PeerRegion, bf16_view, exchange_plan
 
 HEAD_DIM = ops.HEAD_DIM
 
@@ -87,10 +99,22 @@ class HeadShardedFastMKA(nn.Module):
     `groups` maps each sequence group (tuple of ranks) to its torch.distributed
     process group (NCCL); create them on every rank in the same order with
     `make_groups` before the first forward.
+
+    With transport "peer" the returned output is a view of this layer's shared
+    output buffer: it stays valid until the next forward of this module (copy
+    it to keep it longer). The peer exchange needs T divisible by the group
+    size; other lengths take the NCCL all-gather. Call `close()` on every rank
+    before the process group is destroyed.
     """
 
-    def __init__(self, layer: nn.Module, batch: int, rank: int, world_size: int, groups: Optional[dict] = None):
+    def __init__(self, layer: nn.Module, batch: int, rank: int, world_size: int, groups: Optional[dict] = None,
+                 transport: str = "peer"):
         super().__init__()
+        if transport not in ("peer", "nccl"):
+            raise ValueError("transport must be 'peer' or 'nccl'")
+        self.transport = transport
+        self._region: Optional[PeerRegion] = None
+        self._region_key = None
         self.layer = layer
         self.num_heads = getattr(layer, "num_heads", None) or layer.cfg.num_heads
         self.num_kv_heads = getattr(layer, "num_key_value_heads", None) or self.num_heads
@@ -130,19 +154,64 @@ class HeadShardedFastMKA(nn.Module):
                 return fastmka_forward(x, W, self.num_heads, self.num_kv_heads, self.beta, self.use_l3,
                                        l3_memory=l3_memory, rope=rope)["out"]
             B, T, D = x.shape
+            gs = len(self.plan.group)
+            if self.transport == "peer" and B == 1 and T % gs == 0:
+                return self._forward_peer(x, W, hq_r, hkv_r, l3_memory, rope)
             r = fastmka_forward_heads(x, W, hq_r, hkv_r, self.beta, self.use_l3, l3_memory, rope)
             o = r.view(B * T, hq_r * HEAD_DIM)
-            gs = len(self.plan.group)
             flat = torch.empty((gs * B * T, hq_r * HEAD_DIM), dtype=torch.bfloat16, device=x.device)
             dist.all_gather_into_tensor(flat, o, group=self.groups[self.plan.group])
             gathered = flat.view(gs, B * T, hq_r * HEAD_DIM)  # group rank j's heads in block j
             return ops.gemm_kblocked(gathered, W.w_o, W.b_o).view(B, T, D)
+
+    def _peer_region(self, nbytes: int, key, device) -> PeerRegion:
+        if self._region is None or self._region_key != key:
+            if self._region is not None:
+                self._region.close()
+            gs = len(self.plan.group)
+            idx = self.plan.group.index(self.plan.rank)
+            self._region = PeerRegion(self.groups[self.plan.group], idx, gs, nbytes, device)
+            self._region_key = key
+        return self._region
+
+    def _forward_peer(self, x, W, hq_r, hkv_r, l3_memory, rope) -> torch.Tensor:
+        _, T, D = x.shape
+        gs = len(self.plan.group)
+        width = hq_r * HEAD_DIM
+        pl = exchange_plan(gs, self.plan.group.index(self.plan.rank), T, D, width)
+        reg = self._peer_region(pl.nbytes, (T, D, width, str(x.device)), x.device)
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        q, k, v = heads_qkv(x, W, hq_r, hkv_r, self.beta, self.use_l3, l3_memory, rope)
+        # row block j of this rank's attention output -> block `me` of rank j's gather area
+        ops.attn_prefill_scatter(q, k, v, [p + pl.attn_dst_off for p in reg.ptrs], pl.rows,
+                                 (pl.rows * width, width, HEAD_DIM))
+        reg.barrier(stream)  # every rank's rows of this block have landed here
+        gathered = bf16_view(reg.local + pl.gather_off, (gs, pl.rows, width), x.device)
+        # o_proj on this rank's rows, each written into every rank's output
+        ops.gemm_kblocked_scatter(gathered, W.w_o, W.b_o, [p + pl.out_off for p in reg.ptrs], pl.gemm_row0, D)
+        reg.barrier(stream)  # every rank's o_proj rows have landed here
+        return bf16_view(reg.local + pl.out_off, (T, D), x.device).view(1, T, D)
+
+    def close(self) -> None:
+        """Releases the peer buffers (collective over the sequence group)."""
+        if self._region is not None:
+            self._region.close()
+            self._region = None
+            self._region_key = None
 
 
 def fastmka_forward_heads(x: torch.Tensor, W: PreparedWeights, hq: int, hkv: int, beta: float, use_l3: bool,
                           l3_memory: Optional[torch.Tensor], rope) -> torch.Tensor:
     """Stages 1-4 of the layer for a subset of heads (W restricted by shard_weights):
     returns the attention output [B, T, hq, 128]."""
+    q, k, v = heads_qkv(x, W, hq, hkv, beta, use_l3, l3_memory, rope)
+    o, _ = ops.attn_prefill(q, k, v, causal=True, want_lse=False)
+    return o
+
+
+def heads_qkv(x: torch.Tensor, W: PreparedWeights, hq: int, hkv: int, beta: float, use_l3: bool,
+              l3_memory: Optional[torch.Tensor], rope):
+    """Stages 1-3 for a subset of heads: q [B, hq, T, 128] and k, v [B, hkv, T, 128]."""
     B, T, D = x.shape
     xb = x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
     xb = xb.contiguous()
@@ -153,8 +222,7 @@ def fastmka_forward_heads(x: torch.Tensor, W: PreparedWeights, hq: int, hkv: int
     y = ops.gemm(xb.view(B * T, D), W.w_kv)
     y3 = project_l3(l3_memory, W, B, D, hkv, x.device) if use_l3 else None
     k, v, _ = ops.route_ema_blend_kv(y, beta, logits, W.b2, B, T, hkv, bias=W.b_kv, rope=rope, want_lam=False, y3=y3)
-    o, _ = ops.attn_prefill(q, k, v, causal=True, want_lse=False)
-    return o
+    return q, k, v
 
 
 def make_groups(batch: int, num_kv_heads: int, world_size: int) -> dict:

@@ -1,6 +1,8 @@
-"""Head-sharded FastMKA layer on 2 GPUs (NCCL): every rank's output for its
-sequences matches the unsharded layer run on the same sequences. Skipped with
-fewer than 2 GPUs."""
+"""Head-sharded FastMKA layer on 2 GPUs: every rank's output for its sequences
+matches the unsharded layer run on the same sequences, with the exchange done
+by NCCL or by the kernels' own stores into peer memory (three forwards in a
+row for the latter, so that the barriers and the reused buffers are exercised).
+Skipped with fewer than 2 GPUs."""
 import math
 import os
 
@@ -11,7 +13,7 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 
-def _worker(rank, world, port, batch, q):
+def _worker(rank, world, port, batch, transport, q):
     import torch.distributed as dist
     import torch.nn as nn
 
@@ -35,26 +37,35 @@ def _worker(rank, world, port, batch, q):
         ang = torch.cat([pos[:, None] * inv, pos[:, None] * inv], -1)
         rope = (ang.cos()[None], ang.sin()[None])
         groups = make_groups(batch, layer.num_key_value_heads, world)
-        sh = HeadShardedFastMKA(layer, batch, rank, world, groups)
+        sh = HeadShardedFastMKA(layer, batch, rank, world, groups, transport=transport)
         b0, b1 = sh.plan.batch
-        out = sh(x_all[b0:b1].contiguous(), rope=rope)
-        ref = fastmka_forward(x_all[b0:b1].contiguous(), layer.prepared(torch.device("cuda")), layer.num_heads,
+        xs = x_all[b0:b1].contiguous()
+        ref = fastmka_forward(xs, layer.prepared(torch.device("cuda")), layer.num_heads,
                               layer.num_key_value_heads, layer.ema_beta, False, rope=rope)["out"]
-        torch.cuda.synchronize()
-        err = ((out.float() - ref.float()).abs().max() / ref.float().abs().max()).item()
-        q.put((rank, err, len(sh.plan.group), ops.device_status()))
+        errs = []
+        for i in range(3):
+            # a different input each time, so that a stale buffer would show
+            xi = xs if i != 1 else (xs * 0.5).contiguous()
+            out = sh(xi, rope=rope).clone()
+            torch.cuda.synchronize()
+            r = ref if i != 1 else fastmka_forward(xi, layer.prepared(torch.device("cuda")), layer.num_heads,
+                                                    layer.num_key_value_heads, layer.ema_beta, False,
+                                                    rope=rope)["out"]
+            errs.append(((out.float() - r.float()).abs().max() / r.float().abs().max()).item())
+        sh.close()
+        q.put((rank, max(errs), len(sh.plan.group), ops.device_status()))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("batch", [1, 2])
-def test_head_sharded_layer_matches_unsharded(batch):
+@pytest.mark.parametrize("batch,transport", [(1, "peer"), (1, "nccl"), (2, "peer")])
+def test_head_sharded_layer_matches_unsharded(batch, transport):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29100 + batch + os.getpid() % 500
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, batch, q)) for r in range(2)]
+    port = 29100 + 2 * batch + (transport == "peer") + os.getpid() % 500
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, batch, transport, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=180) for _ in range(2)]
