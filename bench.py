@@ -384,8 +384,35 @@ def bench_long_context(args, dist, rank, world, device, peaks):
         step()
     steps = max(3, min(args.steps, 10))
     ms = _timed(dist, step, steps)
-    # this rank's attention kernel alone: its query heads over its sequences
     from mka_b200 import ops
+
+    xk = None
+    if sh._region is not None:
+        # the fused o_proj + all-gather kernel alone, on every rank at once:
+        # this rank's rows of o_proj, stored into every rank's output
+        from mka_b200.peer import bf16_view, exchange_plan
+
+        gs = len(sh.plan.group)
+        W = sh._weights(device)
+        K = W.w_o.shape[1]
+        pl = exchange_plan(gs, sh._region.index, T, D, K // gs)
+        gathered = bf16_view(sh._region.local + pl.gather_off, (gs, pl.rows, K // gs), device)
+        dsts = [p + pl.out_off for p in sh._region.ptrs]
+
+        def xstep():
+            ops.gemm_kblocked_scatter(gathered, W.w_o, W.b_o, dsts, pl.gemm_row0, D)
+
+        xstep()
+        xms = _timed(dist, xstep, steps)
+        xflops = 2.0 * pl.rows * D * K
+        xbytes = (gs - 1) * pl.rows * D * 2
+        target = max(xflops / (peaks["bf16"] * 1e12), xbytes / 770e9) * 1e3
+        xk = {"kernel": "gemm_pair_kernel<scatter>: this rank's o_proj rows stored into every rank's output",
+              "ms": xms, "rows": pl.rows, "flops": xflops, "nvlink_bytes_out": xbytes,
+              "target_ms": round(target, 4), "frac": round(target / xms, 4),
+              "target_basis": "max(FLOPs / measured bf16 burst, bytes out over NVLink / 770 GB/s measured "
+                              "peer copy)"}
+    # this rank's attention kernel alone: its query heads over its sequences
 
     h0, h1 = sh.plan.kv_heads
     hq = (h1 - h0) * (c["H"] // c["HKV"])
@@ -412,6 +439,7 @@ def bench_long_context(args, dist, rank, world, device, peaks):
             "config": {"batch": B, "seq_len": T, "d_model": D, "heads": f"{c['H']}/{c['HKV']}", "levels": 3,
                        "router": f"{D}->{c['R']}->3", "partition": f"sequences x kv heads, group size "
                                                                   f"{gsz}", "exchange": exchange},
+            "exchange_kernel": xk,
             "roofline": {"bound": "tensor", "kernel": "attn_prefill (this rank's heads, T=32768)",
                          "achieved": round(achieved, 1), "peak": peaks["bf16"], "unit": "TFLOP/s",
                          "frac": round(achieved / peaks["bf16"], 4), "peak_kind": f"{peaks['src']} burst bf16",

@@ -13,7 +13,7 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 
-def _worker(rank, world, port, batch, transport, q):
+def _worker(rank, world, port, batch, transport, heads, q):
     import torch.distributed as dist
     import torch.nn as nn
 
@@ -28,8 +28,9 @@ def _worker(rank, world, port, batch, transport, q):
     try:
         from tests.test_parity_gpu import _hf_like_layer
 
-        layer = _hf_like_layer(seed=3)
-        D, T = 512, 640
+        # the router is folded through q_proj, so d_model = query heads x 128
+        layer = _hf_like_layer(seed=3, D=heads[0] * 128, H=heads[0], HKV=heads[1])
+        D, T = heads[0] * 128, 640
         g = torch.Generator(device="cuda").manual_seed(17)
         x_all = (torch.randn(batch, T, D, generator=g, device="cuda") / math.sqrt(D)).bfloat16()
         pos = torch.arange(T, device="cuda").float()
@@ -58,21 +59,23 @@ def _worker(rank, world, port, batch, transport, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("batch,transport", [(1, "peer"), (1, "nccl"), (2, "peer")])
-def test_head_sharded_layer_matches_unsharded(batch, transport):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world,batch,transport,heads", [(2, 1, "peer", (4, 2)), (2, 1, "nccl", (4, 2)),
+                                                        (2, 2, "peer", (4, 2)), (4, 1, "peer", (8, 4)),
+                                                        (4, 2, "peer", (4, 2))])
+def test_head_sharded_layer_matches_unsharded(world, batch, transport, heads):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29100 + 2 * batch + (transport == "peer") + os.getpid() % 500
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, batch, transport, q)) for r in range(2)]
+    port = 29100 + 8 * world + 2 * batch + (transport == "peer") + os.getpid() % 500
+    procs = [ctx.Process(target=_worker, args=(r, world, port, batch, transport, heads, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=180) for _ in range(2)]
+    res = [q.get(timeout=180) for _ in range(world)]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
     for rank, err, gsize, status in res:
         assert status == 0
-        assert gsize == (2 if batch == 1 else 1)
+        assert gsize == max(world // batch, 1)
         assert err < 2e-2
