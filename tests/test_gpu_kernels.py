@@ -250,6 +250,29 @@ def test_attn_decode(ops, B, Hq, Hkv, Tk, splits):
     assert (lse - rlse[..., 0]).abs().max().item() < 2e-2
 
 
+@pytest.mark.parametrize("B,Hq,Hkv,Tq,Tk", [(1, 4, 2, 200, 333), (2, 2, 1, 128, 128), (1, 3, 1, 1, 700)])
+def test_attention_known_answers(ops, B, Hq, Hkv, Tq, Tk):
+    """Closed forms: with every key zero all scores are equal, so a query row
+    that sees n keys has lse = log n and its output is the mean of those value
+    rows, which is the value row itself when the rows are constant per head."""
+    g = torch.Generator(device="cuda").manual_seed(Tq + Tk)
+    q = torch.randn(B, Hq, Tq, 128, device="cuda", generator=g).bfloat16()
+    k = torch.zeros(B, Hkv, Tk, 128, device="cuda").bfloat16()
+    c = torch.randn(B, Hkv, 1, 128, device="cuda", generator=g).bfloat16()
+    v = c.expand(B, Hkv, Tk, 128).contiguous()
+    G = Hq // Hkv
+    want_o = c[:, :, 0].repeat_interleave(G, dim=1)  # [B, Hq, 128]
+    o, lse = ops.attn_prefill(q, k, v, causal=True)
+    n = torch.arange(Tk - Tq + 1, Tk + 1, device="cuda", dtype=torch.float32)  # keys seen by each row
+    assert _rel(o, want_o[:, None].expand(B, Tq, Hq, 128)) < 2e-3
+    assert (lse - n.log()).abs().max().item() < 1e-3
+    if Tq == 1:
+        od, lsed = ops.attn_decode(q, k, v)
+        assert _rel(od[:, 0], want_o) < 2e-3
+        assert (lsed - math.log(Tk)).abs().max().item() < 1e-3
+    assert ops.device_status() == 0
+
+
 @pytest.mark.parametrize("nblk,M,kb,N", [(2, 300, 896, 384), (4, 1024, 128, 512), (1, 77, 256, 256),
                                          (3, 40, 256, 384)])
 def test_gemm_kblocked(ops, nblk, M, kb, N):

@@ -38,6 +38,36 @@ def test_ema_closed_forms():
     _close(orc.causal_prefix_ema(c, beta)[0, :, 1], ref, 1e-6)
 
 
+def test_known_answers_uniform_gate_and_constant_values():
+    """Closed forms that hold for any weights: a zero last router layer gives
+    the uniform gate, so the fused memory is the mean of the levels; with
+    zero keys every visible score is equal, so lse = log(keys seen) and, with
+    every value row equal, the attention output is that row."""
+    import torch.nn.functional as F
+
+    torch.manual_seed(0)
+    b, t, d, heads, r = 2, 16, 64, 2, 32
+    x = torch.randn(b, t, d)
+    l3 = torch.randn(b, t, d)
+    p = {"wq": torch.randn(d, d) / 8, "wk": torch.randn(d, d) / 8, "wv": torch.randn(d, d) / 8, "wo": torch.eye(d),
+         "r1w": torch.randn(r, d) / 8, "r1b": torch.randn(r), "r2w": torch.zeros(3, r), "r2b": torch.zeros(3)}
+    out = orc.fastmka_forward(x, p, heads, True, 0.9, "gelu", l3_memory=l3)
+    _close(out["lam"], torch.full((b, t, 3), 1 / 3), 1e-6)
+    mean = (x + orc.causal_prefix_ema(x, 0.9) + l3) / 3
+    _close(out["k_tot"], F.linear(mean, p["wk"]).view(b, t, heads, d // heads).transpose(1, 2), 1e-5)
+    # attention: zero keys, value rows constant per head; a cache makes the offset nonzero
+    # (the reference takes SDPA only without a cache, fastmka.py:134,157)
+    tk = 12
+    k = torch.zeros(1, 2, tk, 8)
+    c = torch.randn(1, 2, 1, 8)
+    v = c.expand(1, 2, tk, 8)
+    for tq, sdpa in ((12, True), (12, False), (5, False)):
+        q = torch.randn(1, 2, tq, 8)
+        _close(orc.attention(q, k, v, use_sdpa=sdpa), c.expand(1, 2, tq, 8), 1e-6)
+        n = torch.arange(tk - tq + 1, tk + 1, dtype=torch.float32)
+        _close(orc.attention_lse(q, k)[0, 0], n.log(), 1e-6)
+
+
 def _act(case):
     return "gelu" if int(case["act"]) == 1 else "silu"
 
