@@ -562,6 +562,22 @@ def run_kernel_only(args):
                 fn = lambda: ops.kv_proj(x, W.w_kv, W.b_kv, B, T, c["HKV"], rope=(cos, sin))  # noqa: E731
             else:
                 fn = lambda: ops.gemm(x, W.w_o, W.b_o)  # noqa: E731
+    elif args.only in ("o_proj_scatter", "o_proj_blocked"):
+        # o_proj of one rank of a head-sharded group of G ranks (--batch G, default 4) at
+        # the long-context size: T/G rows of the gathered attention output [G, T/G, Hq*128/G].
+        # o_proj_scatter writes every row into G local buffers standing in for the group's
+        # output areas; o_proj_blocked is the plain blocked GEMM on the same operands.
+        G = args.batch or 4
+        cl = LONG
+        rows, width = cl["T"] // G, cl["H"] * 128 // G
+        a = torch.randn(G, rows, width, generator=g, device=dev).to(torch.bfloat16)
+        w = (torch.randn(cl["D"], G * width, generator=g, device=dev) / 60).to(torch.bfloat16)
+        if args.only == "o_proj_scatter":
+            outs = [torch.empty(cl["T"], cl["D"], device=dev, dtype=torch.bfloat16) for _ in range(G)]
+            ptrs = [o.data_ptr() for o in outs]
+            fn = lambda: ops.gemm_kblocked_scatter(a, w, None, ptrs, 0, cl["D"])  # noqa: E731
+        else:
+            fn = lambda: ops.gemm_kblocked(a, w)  # noqa: E731
     elif args.only == "attn_decode":
         B = args.batch or d["B"]
         q = torch.randn(B, d["H"], 1, 128, generator=g, device=dev, dtype=torch.bfloat16)
@@ -570,10 +586,16 @@ def run_kernel_only(args):
         fn = lambda: ops.attn_decode(q, k, v)  # noqa: E731
     else:
         raise SystemExit(f"unknown kernel {args.only}")
-    for _ in range(n):
+    for _ in range(args.warmup):
         fn()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        fn()
+    e1.record()
     torch.cuda.synchronize()
-    print(json.dumps({"only": args.only, "launches": n, "device_status": ops.device_status()}))
+    print(json.dumps({"only": args.only, "launches": n, "ms_per_launch": e0.elapsed_time(e1) / max(args.steps, 1),
+                      "device_status": ops.device_status()}))
 
 
 def _config(args):
@@ -668,7 +690,7 @@ def main():
                     help="skip the full Llama-3-8B model measurement (one GPU only)")
     ap.add_argument("--only", default=None,
                     help="run one kernel alone (attn_prefill, attn_decode, route_ema_blend, route_ema_blend_h, "
-                         "qr_proj, kv_gemm, kv_proj, o_proj)")
+                         "qr_proj, kv_gemm, kv_proj, o_proj, o_proj_scatter, o_proj_blocked)")
     ap.add_argument("--batch", type=int, default=0, help="batch override for --only")
     args = ap.parse_args()
     if args.only:
