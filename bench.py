@@ -614,11 +614,13 @@ MODEL = dict(name="Llama-3-8B", vocab=128256, D=4096, FFN=14336, layers=32, H=32
 def bench_model(args, device):
     """The whole Llama-3-8B architecture from transformers (random bf16 weights,
     N(0, 0.02)) with every self_attn replaced by the FastMKA module through the
-    reference's patch API, one prefill forward of a 65536-token sequence per
-    step (logits of the last position only). Also times one patched self_attn
-    alone at that length, the part of each layer this package replaces."""
+    reference's patch API (and, with --model-mlp fused, every MLP by the fused
+    SwiGLU MLP), one prefill forward of a 65536-token sequence per step (logits
+    of the last position only). Also times one patched self_attn alone at that
+    length, the part of each layer this package replaces."""
     from transformers import LlamaConfig, LlamaForCausalLM
 
+    from mka_b200.hf.mlp import apply_mlp_fusion
     from mka_b200.hf.patch import HFPatchConfig, apply_hf_attention_patch
 
     c = MODEL
@@ -632,6 +634,7 @@ def bench_model(args, device):
             torch.manual_seed(5)
             model = LlamaForCausalLM(cfg).eval()
             patched = apply_hf_attention_patch(model, HFPatchConfig(verbose=False))
+            fused_mlp = apply_mlp_fusion(model) if args.model_mlp == "fused" else 0
     finally:
         torch.set_default_dtype(prev)
     g = torch.Generator(device=device).manual_seed(6)
@@ -661,13 +664,15 @@ def bench_model(args, device):
     out = {
         "metric": "Llama-3-8B prefill tokens/s, every self_attn patched with FastMKA (transformers model)",
         "value": tokens / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
-        "patched_layers": patched,
+        "patched_layers": patched, "fused_mlp_layers": fused_mlp,
         "fastmka_self_attn_ms_per_layer": attn_ms,
         "fastmka_self_attn_share": round(attn_ms * c["layers"] / ms, 4),
         "attention_tflops_per_layer": attn_flops / 1e12,
         "config": {"model": c["name"], "layers": c["layers"], "d_model": c["D"], "ffn": c["FFN"],
                    "heads": f"{c['H']}/{c['HKV']}", "vocab": c["vocab"], "rope_theta": c["theta"],
-                   "batch": c["B"], "seq_len": c["T"], "logits": "last position"},
+                   "batch": c["B"], "seq_len": c["T"], "logits": "last position",
+                   "mlp": ("gate/up GEMM with the SiLU-product epilogue, then down_proj (FusedSwiGLUMLP)"
+                           if fused_mlp else "transformers LlamaMLP (cuBLAS GEMMs + elementwise)")},
         "data": "synthetic token ids U[0, vocab), random N(0, 0.02) bf16 weights",
     }
     del model
@@ -686,6 +691,8 @@ def main():
     ap.add_argument("--no-long", action="store_true", help="skip the long-context (L3, seq 32768) measurement")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="how a head-sharded sequence group exchanges rows (long context, N > 2)")
+    ap.add_argument("--model-mlp", choices=["fused", "transformers"], default="transformers",
+                    help="the full-model line's MLP: transformers' own (default) or the fused SwiGLU GEMM")
     ap.add_argument("--no-model", action="store_true",
                     help="skip the full Llama-3-8B model measurement (one GPU only)")
     ap.add_argument("--only", default=None,

@@ -38,6 +38,9 @@
  *                           (fastmka.py:175-176; hf/attention.py:194-195)
  *   fmka_get_last_error     the TORCH_CHECK / cudaGetLastError error reporting of
  *                           fastmka_attn.cu:134-150,169-170
+ *   fmka_gemm_bf16_swiglu   outside the attention path: the gate/up projections and
+ *                           SiLU product of the Llama MLP around the patched
+ *                           self_attn (transformers LlamaMLP), one GEMM
  *   fmka_attn_fwd_prefill_scatter, fmka_gemm_bf16_kblocked_scatter, fmka_peer_*
  *                           the head-sharded layer over several GPUs of a box:
  *                           attention rows and o_proj rows stored straight into
@@ -232,6 +235,15 @@ FMKA_API int fmka_attn_decode_splitkv(const void* q, int64_t q_sb, int64_t q_sh,
                              int64_t kv_sh, int64_t kv_st, void* o, int64_t o_sb, int64_t o_sh, float* lse,
                              int64_t lse_sb, int B, int Hq, int Hkv, int Tk, int head_dim, float scale,
                              int num_splits, void* workspace, size_t workspace_bytes, fmka_stream_t stream);
+
+/* SwiGLU feed-forward input projection (the gate_proj / up_proj / act_fn of a
+ * Llama MLP, fused): c[m, i] = silu(a w_g[i]^T + b_g[i]) * (a w_u[i]^T + b_u[i])
+ * for i < I, bf16 out with fp32 accumulation. w_gu [2I, K] holds the two
+ * weights interleaved in blocks of 128 rows: rows 256j .. 256j+127 are gate
+ * rows 128j .. 128j+127 and rows 256j+128 .. 256j+255 the matching up rows
+ * (bias_gu [2I] fp32 in the same order, or NULL). I must be a multiple of 128. */
+FMKA_API int fmka_gemm_bf16_swiglu(const void* a, int64_t lda, const void* w_gu, int64_t ldw, const float* bias_gu,
+                          void* c, int64_t ldc, int M, int I, int K, fmka_stream_t stream);
 
 /* ------------------------------------------------ several GPUs of a box ---
  * The ranks of a sequence group (one process per GPU) share buffers through

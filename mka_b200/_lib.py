@@ -26,6 +26,7 @@ _SIGNATURES = {
     "fmka_num_sms": (_I, []),
     "fmka_gemm_bf16": (_I, [_P, _L, _P, _L, _P, _P, _L, _I, _I, _I, _P]),
     "fmka_gemm_bf16_kblocked": (_I, [_P, _I, _L, _L, _P, _L, _P, _P, _L, _I, _I, _I, _P]),
+    "fmka_gemm_bf16_swiglu": (_I, [_P, _L, _P, _L, _P, _P, _L, _I, _I, _I, _P]),
     "fmka_qr_proj": (_I, [_P, _L, _P, _L, _P, _I, _I, _I, _I, _I, _P, _L, _L, _L, _I,
                           _P, _P, _L, _L, _P, _I, _I, _P, _P]),
     "fmka_kv_proj": (_I, [_P, _L, _P, _L, _P, _I, _I, _I, _I, _P, _P, _L, _L, _L, _I,

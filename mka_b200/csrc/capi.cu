@@ -246,6 +246,31 @@ int fmka_gemm_bf16_kblocked(const void* a, int a_kblk, int64_t a_blk_stride, int
   return launch_gemm(bf(a), lda, bf(w), ldw, p, num_sms_current_device(), as_stream(stream));
 }
 
+int fmka_gemm_bf16_swiglu(const void* a, int64_t lda, const void* w_gu, int64_t ldw, const float* bias_gu, void* c,
+                          int64_t ldc, int M, int I, int K, fmka_stream_t stream) {
+  if (a == nullptr || w_gu == nullptr || c == nullptr) return set_error(kErrInvalidArgument, "gemm_swiglu: null pointer");
+  if (I <= 0 || I % 128 != 0)
+    return set_error(kErrInvalidArgument, "gemm_swiglu: the channel count must be a positive multiple of 128");
+  if (bias_gu != nullptr && !al16(bias_gu))
+    return set_error(kErrInvalidArgument, "gemm_swiglu: bias must be 16-byte aligned");
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = M;
+  p.N = 2 * I;
+  p.K = K;
+  p.n_split = 2 * I;
+  p.seg[0] = empty_seg();
+  p.seg[0].kind = kSegSwiGLU;
+  p.seg[0].n_begin = 0;
+  p.seg[0].n_end = 2 * I;
+  p.seg[0].out = bfw(c);
+  p.seg[0].ld = ldc;
+  p.seg[0].bias = bias_gu;
+  p.seg[1] = empty_seg();
+  p.status = device_status_word();
+  return launch_gemm(bf(a), lda, bf(w_gu), ldw, p, num_sms_current_device(), as_stream(stream));
+}
+
 int fmka_qr_proj(const void* x, int64_t ldx, const void* w_qr, int64_t ldw, const float* bias_qr, int B, int T,
                  int D, int Hq, int R, void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, int t_offset,
                  const float* rope_cos, const float* rope_sin, int64_t rope_sb, int64_t rope_st, const float* w2,

@@ -44,7 +44,7 @@ struct PeerPtrs {
 };
 
 // ------------------------------------------------------------------- GEMM --
-enum SegKind : int { kSegRowMajor = 0, kSegHeads = 1, kSegRouter = 2 };
+enum SegKind : int { kSegRowMajor = 0, kSegHeads = 1, kSegRouter = 2, kSegSwiGLU = 3 };
 
 struct GemmSeg {
   int kind;
@@ -64,6 +64,8 @@ struct GemmSeg {
   int L;
   int act;               // 0 = SiLU, 1 = GELU (erf)
   float* logits;         // [M, L] fp32, accumulated
+  // SwiGLU: columns come in blocks of 256, gate rows then up rows of the same
+  // 128 output channels; out [M, ld] receives silu(gate) * up per channel.
 };
 
 struct GemmParams {

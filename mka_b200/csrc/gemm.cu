@@ -182,6 +182,35 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams& p, int m, b
         }
       }
     }
+  } else if (sg.kind == kSegSwiGLU) {
+    // Tile columns n0 .. n0+127 are gate rows and n0+128 .. n0+255 the up rows
+    // of output channels (n0 - n_begin) / 2 .. + 127 (256-wide tiles only).
+    if constexpr (BN == 256) {
+      const int oc0 = (n0 - sg.n_begin) / 2;
+      const bool in_range = n0 < sg.n_end;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t g[32], u[32];
+        tmem_ld32(acc_addr + c * 32, g);
+        tmem_ld32(acc_addr + 128 + c * 32, u);
+        tmem_wait_ld();
+        if (row_ok && in_range) {
+          const int nl = n0 - sg.n_begin + c * 32;
+          uint32_t r[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float gv = __uint_as_float(g[j]);
+            float uv = __uint_as_float(u[j]);
+            if (sg.bias != nullptr) {
+              gv += __ldg(sg.bias + nl + j);
+              uv += __ldg(sg.bias + nl + 128 + j);
+            }
+            r[j] = __float_as_uint(act_fn(gv, 0) * uv);
+          }
+          store_row32(sg.out + (int64_t)m * sg.ld + oc0 + c * 32, r, 32);
+        }
+      }
+    }
   } else {  // kSegRouter
     float part[4] = {0.f, 0.f, 0.f, 0.f};
     const int R = sg.n_end - sg.n_begin;
@@ -915,8 +944,14 @@ int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int
   int BN = 256;
   if (p.n_split % 256 != 0 && p.n_split < p.N) BN = 128;
   // One row block (decode-sized M): the GEMM streams weights, and narrower
-  // tiles double the number of CTAs pulling them.
-  if (p.M <= kBM) BN = 128;
+  // tiles double the number of CTAs pulling them. The SwiGLU epilogue needs a
+  // tile to hold both halves of a 256-column block.
+  const bool swiglu = p.seg[0].kind == kSegSwiGLU;
+  if (p.M <= kBM && !swiglu) BN = 128;
+  if (swiglu && (p.N % 256 != 0 || p.n_split < p.N || p.seg[0].ld % 8 != 0 ||
+                 (reinterpret_cast<uintptr_t>(p.seg[0].out) & 15u)))
+    return set_error(kErrInvalidArgument,
+                     "gemm: SwiGLU needs N a multiple of 256, one segment, a 16-byte aligned output");
   if (p.n_split % 128 != 0 && p.n_split < p.N)
     return set_error(kErrInvalidArgument, "gemm: segment split must be a multiple of 128 columns");
   // Scatter epilogue: always the CTA-pair kernel with 256-wide tiles.

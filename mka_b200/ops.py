@@ -119,6 +119,38 @@ def gemm_kblocked(a_blocks: torch.Tensor, w: torch.Tensor, bias: Optional[torch.
     return out
 
 
+def interleave_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
+    """[2I, K] weight for gemm_swiglu from gate_proj / up_proj weights [I, K]:
+    blocks of 128 gate rows followed by the matching 128 up rows. Also works
+    on biases ([I] -> [2I])."""
+    if w_gate.shape != w_up.shape or w_gate.shape[0] % 128:
+        raise RuntimeError("interleave_gate_up: gate and up must match, with a multiple of 128 rows")
+    I = w_gate.shape[0]
+    rest = tuple(w_gate.shape[1:])
+    return torch.stack([w_gate.reshape(I // 128, 128, *rest), w_up.reshape(I // 128, 128, *rest)], 1).reshape(
+        2 * I, *rest).contiguous()
+
+
+def gemm_swiglu(x: torch.Tensor, w_gu: torch.Tensor, bias_gu: Optional[torch.Tensor] = None,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[M, I] = silu(x w_gate^T + b_gate) * (x w_up^T + b_up) in one GEMM, with
+    w_gu (and bias_gu) from interleave_gate_up."""
+    _check_cuda(x, w_gu)
+    _check_bf16(x, w_gu)
+    if x.dim() != 2 or w_gu.dim() != 2 or x.shape[1] != w_gu.shape[1] or w_gu.shape[0] % 256:
+        raise RuntimeError("gemm_swiglu: expected x [M, K] and w_gu [2I, K] with I a multiple of 128")
+    if x.stride(1) != 1 or w_gu.stride(1) != 1:
+        raise RuntimeError("gemm_swiglu: inner dimension must be contiguous")
+    M, K = x.shape
+    I = w_gu.shape[0] // 2
+    if out is None:
+        out = torch.empty((M, I), dtype=torch.bfloat16, device=x.device)
+    b32 = _f32(bias_gu)
+    _lib.call("fmka_gemm_bf16_swiglu", x.data_ptr(), x.stride(0), w_gu.data_ptr(), w_gu.stride(0), _ptr(b32),
+              out.data_ptr(), out.stride(0), M, I, K, _stream(x))
+    return out
+
+
 def gemm_kblocked_scatter(a_blocks: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
                           dst_ptrs: Sequence[int], row0: int, ldc: int) -> None:
     """gemm_kblocked whose output row m goes to row row0 + m of every buffer in

@@ -273,6 +273,27 @@ def test_attention_known_answers(ops, B, Hq, Hkv, Tq, Tk):
     assert ops.device_status() == 0
 
 
+@pytest.mark.parametrize("M,I,K,bias", [(1, 128, 256, False), (64, 384, 512, True), (100, 1408, 256, False),
+                                        (300, 256, 1024, True), (1000, 1408, 512, False)])
+def test_gemm_swiglu(ops, M, I, K, bias):
+    """silu(x Wg^T + bg) * (x Wu^T + bu) from one GEMM over the interleaved weight."""
+    g = torch.Generator(device="cuda").manual_seed(M + I + K)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    wg = (torch.randn(I, K, device="cuda", generator=g) / math.sqrt(K)).bfloat16()
+    wu = (torch.randn(I, K, device="cuda", generator=g) / math.sqrt(K)).bfloat16()
+    bg = torch.randn(I, device="cuda", generator=g) if bias else None
+    bu = torch.randn(I, device="cuda", generator=g) if bias else None
+    w_gu = ops.interleave_gate_up(wg, wu)
+    b_gu = ops.interleave_gate_up(bg, bu) if bias else None
+    out = ops.gemm_swiglu(x, w_gu, b_gu)
+    gate = x.float() @ wg.float().t() + (bg if bias else 0.0)
+    up = x.float() @ wu.float().t() + (bu if bias else 0.0)
+    ref = torch.nn.functional.silu(gate) * up
+    assert out.shape == (M, I)
+    assert ops.device_status() == 0
+    assert _rel(out, ref) < 1e-2
+
+
 @pytest.mark.parametrize("nblk,M,kb,N", [(2, 300, 896, 384), (4, 1024, 128, 512), (1, 77, 256, 256),
                                          (3, 40, 256, 384)])
 def test_gemm_kblocked(ops, nblk, M, kb, N):

@@ -120,3 +120,41 @@ def test_patched_llama_prefill_and_cached_decode():
         k_ref = rkv.layers[1].keys
         assert k_gpu.shape == k_ref.shape == (2, 1, 98, 128)
         assert _rel(k_gpu, k_ref) < 3e-2
+
+
+def test_mlp_fusion_walks_layers_and_keeps_parameter_names():
+    """Host logic only: every gated SiLU MLP is replaced, the state_dict keys
+    and tensors are unchanged, and a second call changes nothing."""
+    from mka_b200.hf.mlp import FusedSwiGLUMLP, apply_mlp_fusion
+
+    model = _tiny_llama()
+    keys = {k: v.clone() for k, v in model.state_dict().items()}
+    assert apply_mlp_fusion(model) == 2
+    assert all(isinstance(layer.mlp, FusedSwiGLUMLP) for layer in model.model.layers)
+    after = model.state_dict()
+    assert set(after) == set(keys)
+    assert all(torch.equal(after[k], keys[k]) for k in keys)
+    assert apply_mlp_fusion(model) == 0
+
+
+@pytest.mark.gpu
+def test_fused_mlp_matches_transformers_mlp():
+    """A patched LlamaForCausalLM with the fused MLP against the same model with
+    transformers' MLP (both bf16 on the GPU, self_attn patched in both)."""
+    from mka_b200.hf.mlp import FusedSwiGLUMLP, apply_mlp_fusion
+
+    model = _tiny_llama().to(torch.bfloat16)
+    assert apply_hf_attention_patch(model, HFPatchConfig(verbose=False)) == 2
+    model = model.to("cuda")
+    fused = copy.deepcopy(model)
+    assert apply_mlp_fusion(fused) == 2
+    g = torch.Generator().manual_seed(3)
+    x = (torch.randn(2, 96, 256, generator=g) * 0.5).bfloat16().cuda()
+    with torch.no_grad():
+        mlp = model.model.layers[0].mlp
+        fm = FusedSwiGLUMLP(mlp)
+        assert _rel(fm(x), mlp(x)) < 2e-2
+        ids = torch.randint(0, 128, (2, 96), generator=g).cuda()
+        a = model(ids).logits
+        b = fused(ids).logits
+    assert _rel(b, a) < 2e-2
