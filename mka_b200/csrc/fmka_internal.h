@@ -82,7 +82,23 @@ struct GemmParams {
   int64_t dst_row0;
   int64_t dst_ld;
   PeerPtrs dst;
+  // Tile order (set by launch_gemm): bands of raster_group row blocks with the
+  // row block running fastest inside a band; 1 is plain row-major order.
+  int raster_group;
 };
+
+// Row block mb and column block nb of persistent-GEMM tile `tile` (see
+// GemmParams::raster_group); a bijection of [0, num_m * num_n) onto the grid.
+__host__ __device__ __forceinline__ void gemm_tile_coords(int tile, int num_m, int num_n, int group, int& mb,
+                                                          int& nb) {
+  const int band_tiles = group * num_n;
+  const int band = tile / band_tiles;
+  const int first = band * group;
+  const int rows = group < num_m - first ? group : num_m - first;
+  const int r = tile - band * band_tiles;
+  mb = first + r % rows;
+  nb = r / rows;
+}
 
 // C = A[M,K] * B[N,K]^T with the segment epilogues. A and B are row-major bf16
 // with row strides lda / ldb (elements).

@@ -396,8 +396,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       long issued = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-        const int m0 = (tile / num_n) * kBM;
-        const int n0 = (tile % num_n) * BN;
+        int mb, nb;
+        gemm_tile_coords(tile, num_m, num_n, p.raster_group, mb, nb);
+        const int m0 = mb * kBM;
+        const int n0 = nb * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
             *abort_flag = 1;
@@ -488,8 +490,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int m0 = (tile / num_n) * kBM;
-      const int n0 = (tile % num_n) * BN;
+      int mb, nb;
+      gemm_tile_coords(tile, num_m, num_n, p.raster_group, mb, nb);
+      const int m0 = mb * kBM;
+      const int n0 = nb * BN;
       const int m = m0 + row_in_tile;
       const bool row_ok = m < p.M;
       gemm_epilogue_tile<BN>(p, m, row_ok, n0, lane_addr + acc * BN);
@@ -602,8 +606,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       long issued = 0;
       for (int tile = pair; tile < num_tiles && !*abort_flag; tile += npairs) {
-        const int m0 = (tile / num_n) * (2 * kBM) + (int)rank * kBM;
-        const int n0 = (tile % num_n) * BN + (int)rank * Cfg::kHalfN;
+        int mb, nb;
+        gemm_tile_coords(tile, num_m, num_n, p.raster_group, mb, nb);
+        const int m0 = mb * (2 * kBM) + (int)rank * kBM;
+        const int n0 = nb * BN + (int)rank * Cfg::kHalfN;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
             *abort_flag = 1;
@@ -695,8 +701,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int m = (tile / num_n) * (2 * kBM) + (int)rank * kBM + row_in_tile;
-      const int n0 = (tile % num_n) * BN;
+      int mb, nb;
+      gemm_tile_coords(tile, num_m, num_n, p.raster_group, mb, nb);
+      const int m = mb * (2 * kBM) + (int)rank * kBM + row_in_tile;
+      const int n0 = nb * BN;
       if constexpr (kScatter)
         gemm_epilogue_scatter<BN>(p, m - lane, n0, lane_addr + acc * BN,
                                   sScatter + ew * (kScatterWarpBytes / 16));
@@ -932,9 +940,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int64_t ldb, const GemmParams& p,
+int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int64_t ldb, const GemmParams& p_in,
                 int num_sms, cudaStream_t stream) {
+  GemmParams p = p_in;
   if (p.M <= 0 || p.N <= 0 || p.K <= 0) return set_error(kErrInvalidArgument, "gemm: M, N, K must be positive");
+  // Tile order. A weight that fits comfortably in L2 (every projection of the
+  // attention layer: at most 29 MB) stays there whatever the order, and the
+  // tiles go row-major. A larger one would stream from HBM once per row
+  // block, so its tiles go in bands of 8 row blocks, each weight tile reused
+  // across the band while it is in L2.
+  p.raster_group = ((int64_t)p.N * p.K * 2 > (int64_t(64) << 20)) ? 8 : 1;
   if (p.K % 8 != 0 || lda % 8 != 0 || ldb % 8 != 0)
     return set_error(kErrInvalidArgument, "gemm: K and row strides must be multiples of 8 elements");
   if ((reinterpret_cast<uintptr_t>(A) & 15u) || (reinterpret_cast<uintptr_t>(B) & 15u))
