@@ -614,10 +614,13 @@ MODEL = dict(name="Llama-3-8B", vocab=128256, D=4096, FFN=14336, layers=32, H=32
 def bench_model(args, device):
     """The whole Llama-3-8B architecture from transformers (random bf16 weights,
     N(0, 0.02)) with every self_attn replaced by the FastMKA module through the
-    reference's patch API (and, with --model-mlp fused, every MLP by the fused
-    SwiGLU MLP), one prefill forward of a 65536-token sequence per step (logits
-    of the last position only). Also times one patched self_attn alone at that
-    length, the part of each layer this package replaces."""
+    reference's patch API with three levels (L1 + L2 + L3; the L3 memory is one
+    seeded N(0, 0.5) [1, 65536, 4096] tensor passed with the model call, which
+    transformers forwards to every self_attn), and with --model-mlp fused every
+    MLP by the fused SwiGLU MLP; one prefill forward of a 65536-token sequence
+    per step (logits of the last position only). Also times one patched
+    self_attn alone at that length, the part of each layer this package
+    replaces."""
     from transformers import LlamaConfig, LlamaForCausalLM
 
     from mka_b200.hf.mlp import apply_mlp_fusion
@@ -633,16 +636,17 @@ def bench_model(args, device):
         with torch.device(device):
             torch.manual_seed(5)
             model = LlamaForCausalLM(cfg).eval()
-            patched = apply_hf_attention_patch(model, HFPatchConfig(verbose=False))
+            patched = apply_hf_attention_patch(model, HFPatchConfig(use_l3=True, verbose=False))
             fused_mlp = apply_mlp_fusion(model) if args.model_mlp == "fused" else 0
     finally:
         torch.set_default_dtype(prev)
     g = torch.Generator(device=device).manual_seed(6)
     ids = torch.randint(0, c["vocab"], (c["B"], c["T"]), generator=g, device=device)
+    l3 = (torch.randn(c["B"], c["T"], c["D"], generator=g, device=device) * 0.5).to(torch.bfloat16)
 
     def step():
         with torch.no_grad():
-            model(ids, use_cache=False, logits_to_keep=1)
+            model(ids, use_cache=False, logits_to_keep=1, l3_memory=l3)
 
     step()  # warm-up: first call also folds and caches each layer's weights
     steps = max(1, min(args.steps, 3))
@@ -655,7 +659,7 @@ def bench_model(args, device):
 
     def attn_step():
         with torch.no_grad():
-            attn(hidden_states=x, position_embeddings=pe)
+            attn(hidden_states=x, position_embeddings=pe, l3_memory=l3)
 
     attn_step()
     attn_ms = _timed(None, attn_step, steps)
@@ -671,6 +675,7 @@ def bench_model(args, device):
         "config": {"model": c["name"], "layers": c["layers"], "d_model": c["D"], "ffn": c["FFN"],
                    "heads": f"{c['H']}/{c['HKV']}", "vocab": c["vocab"], "rope_theta": c["theta"],
                    "batch": c["B"], "seq_len": c["T"], "logits": "last position",
+                   "levels": "L1 + L2 + L3 (L3: seeded N(0, 0.5) memory [1, 65536, 4096], the same for every layer)",
                    "mlp": ("gate/up GEMM with the SiLU-product epilogue, then down_proj (FusedSwiGLUMLP)"
                            if fused_mlp else "transformers LlamaMLP (cuBLAS GEMMs + elementwise)")},
         "data": "synthetic token ids U[0, vocab), random N(0, 0.02) bf16 weights",
@@ -729,7 +734,11 @@ def main():
     model = None
     if not args.no_model:
         if world == 1:
-            model = bench_model(args, device)
+            try:
+                model = bench_model(args, device)
+            except Exception as e:  # a secondary line must not take the headline line down with it
+                model = {"error": f"{type(e).__name__}: {e}"[:400]}
+                torch.cuda.empty_cache()
         else:
             model = {"skipped": "the full-model line runs on one GPU (its FFN and embeddings are not sharded)"}
     status = ops.device_status()
