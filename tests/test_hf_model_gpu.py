@@ -158,3 +158,28 @@ def test_fused_mlp_matches_transformers_mlp():
         a = model(ids).logits
         b = fused(ids).logits
     assert _rel(b, a) < 2e-2
+
+
+def test_l3_memory_reaches_every_patched_layer(monkeypatch):
+    """Host logic only: an L3 memory passed with the model call (the three-level
+    full-model configuration) arrives at every patched self_attn's
+    forward_with_lse, unchanged, next to the model's own RoPE tables."""
+    if not _two_value_attention_api():
+        pytest.skip("needs the transformers >= 4.48 self_attn protocol")
+    model = _tiny_llama()
+    assert apply_hf_attention_patch(model, HFPatchConfig(use_l3=True, verbose=False)) == 2
+    seen = []
+
+    def fake(self, hidden_states, attention_mask=None, position_ids=None, past_key_value=None,
+             output_attentions=False, use_cache=False, cache_position=None, position_embeddings=None,
+             l3_memory=None, **kw):
+        seen.append((self.layer_idx, l3_memory, position_embeddings is not None))
+        return hidden_states, None, None, None, None
+
+    monkeypatch.setattr(HFFastMKAAttention, "forward_with_lse", fake)
+    r = torch.randn(1, 12, 256)
+    with torch.no_grad():
+        model(torch.randint(0, 128, (1, 12)), use_cache=False, logits_to_keep=1, l3_memory=r)
+    assert [s[0] for s in seen] == [0, 1]
+    assert all(s[1] is r and s[2] for s in seen)
+    assert all(layer.self_attn.use_l3 for layer in model.model.layers)
