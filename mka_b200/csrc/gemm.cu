@@ -990,6 +990,11 @@ int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int
       return set_error(kErrInvalidArgument, "gemm: router epilogue needs 1..4 levels, w2 and logits");
     if (g.kind == kSegRowMajor && (g.ld % 8 != 0))
       return set_error(kErrInvalidArgument, "gemm: output row stride must be a multiple of 8");
+    // an output row must not run into the next one
+    if (p.n_dst == 0 && g.kind == kSegRowMajor && g.ld < g.n_end - g.n_begin)
+      return set_error(kErrInvalidArgument, "gemm: output row stride is smaller than the row");
+    if (g.kind == kSegSwiGLU && g.ld < (g.n_end - g.n_begin) / 2)
+      return set_error(kErrInvalidArgument, "gemm: output row stride is smaller than the row");
   }
 
   CUtensorMap tmA, tmB;

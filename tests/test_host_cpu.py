@@ -49,6 +49,33 @@ def test_argument_errors_are_status_codes():
                   None, None, 0, None)
 
 
+def test_argument_errors_of_the_newer_entry_points():
+    """Checked on the host before any device work, so they run without a GPU:
+    rows that would overlap, the SwiGLU channel rule, scatter destination
+    counts and coverage, and the barrier's rank / group size."""
+    from mka_b200 import _lib
+
+    lib = _lib.load()
+    P = ctypes.c_void_p
+    a, w, c = P(1 << 12), P(1 << 13), P(1 << 14)  # aligned addresses; nothing is launched
+    rc = lib.fmka_gemm_bf16(a, 64, w, 64, None, c, 32, 128, 64, 64, None)  # ldc 32 < N 64
+    assert rc == 1 and "row stride" in _lib.last_error()[1]
+    rc = lib.fmka_gemm_bf16_swiglu(a, 64, w, 64, None, c, 192, 128, 192, 64, None)  # I = 192
+    assert rc == 1 and "multiple of 128" in _lib.last_error()[1]
+    rc = lib.fmka_gemm_bf16_swiglu(a, 64, w, 64, None, c, 64, 128, 128, 64, None)  # ldc 64 < I 128
+    assert rc == 1 and "row stride" in _lib.last_error()[1]
+    dsts = (P * 9)(*([c] * 9))
+    rc = lib.fmka_gemm_bf16_kblocked_scatter(a, 64, 128 * 64, 64, w, 128, None, dsts, 9, 0, 128, 128, 128, 128, None)
+    assert rc == 1 and "1 to 8" in _lib.last_error()[1]
+    rc = lib.fmka_attn_fwd_prefill_scatter(a, 0, 0, 128, w, w, 0, 0, 128, dsts, 2, 100, 0, 256, 128,
+                                           1, 2, 1, 300, 300, 128, 1, 0.1, None)  # 2 x 100 rows < 300
+    assert rc == 1 and "cover" in _lib.last_error()[1]
+    flags = (P * 2)(c, c)
+    assert lib.fmka_peer_barrier(flags, 2, 2, 1, None) == 1  # rank outside the group
+    assert lib.fmka_peer_barrier(flags, 0, 9, 1, None) == 1  # more than 8 ranks
+    assert lib.fmka_peer_alloc(0, ctypes.byref(P())) == 1
+
+
 def test_workspace_sizes():
     from mka_b200 import _lib
 
