@@ -174,3 +174,33 @@ def test_prepared_weights_fold_router_through_q():
     router[1] = nn.Tanh()
     with pytest.raises(NotImplementedError):
         prepare(wq, wk, wv, wo, router, torch.device("cpu"))
+
+
+def test_static_kv_cache_bookkeeping():
+    """Host logic of the in-place decode cache (buffers on the CPU here): one
+    slot per attention module in call order, lengths, the capacity and layer
+    limits, prefix loading, and the EMA state ping-pong of carry_ema."""
+    from mka_b200 import StaticKVCache
+
+    c = StaticKVCache(batch=2, num_kv_heads=1, capacity=8, num_layers=2, device="cpu", carry_ema=True)
+    a, b, extra = nn.Linear(1, 1), nn.Linear(1, 1), nn.Linear(1, 1)
+    ka, _ = c.layer(a)
+    kb, _ = c.layer(b)
+    assert ka.data_ptr() != kb.data_ptr() and c.layer(a)[0].data_ptr() == ka.data_ptr()
+    with pytest.raises(RuntimeError):
+        c.layer(extra)  # more attention modules than layers
+    c.advance(a, 5)
+    assert c.length(a) == 5 and c.length(b) == 0
+    with pytest.raises(RuntimeError):
+        c.advance(a, 4)  # 9 > capacity 8
+    assert c.length(a) == 5
+    k = torch.randn(2, 1, 3, 128).bfloat16()
+    c.load_prefix(1, k, -k)
+    assert c.length(b) == 3 and torch.equal(c.k[1][:, :, :3], k) and torch.equal(c.v[1][:, :, :3], -k)
+    s_in, s_out = c.ema_buffers(a, 256, "cpu")
+    assert s_in.shape == (2, 256) and s_in.dtype == torch.float32 and not s_in.any()
+    s_out.fill_(1.0)
+    c.commit_ema(a)
+    s_in2, s_out2 = c.ema_buffers(a, 256, "cpu")
+    assert s_in2.data_ptr() == s_out.data_ptr() and s_out2.data_ptr() == s_in.data_ptr()
+    assert bool((s_in2 == 1.0).all())
