@@ -99,6 +99,16 @@ def test_ops_refuse_cpu_tensors():
         ops.attn_prefill(q, q, q)
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.causal_prefix_ema(torch.zeros(1, 4, 8, dtype=torch.bfloat16))
+    # the reference's op API (mka/cuda/ops.py): same probes, same RuntimeError on CPU inputs
+    from mka_b200 import cuda as mka_cuda
+
+    assert mka_cuda.has_fastmka_cuda() == torch.cuda.is_available()
+    assert mka_cuda.has_fused_route_mka_cuda() == torch.cuda.is_available()
+    with pytest.raises(RuntimeError):
+        mka_cuda.fastmka_attn(q, q, q)
+    x = torch.zeros(1, 128, 128)
+    with pytest.raises(RuntimeError):
+        mka_cuda.fused_route_mka_attn(q, x, x, x, torch.zeros(1, 128, 2), torch.zeros(128, 128), torch.zeros(128, 128))
 
 
 def test_fastmka_module_matches_reference_parameters():
