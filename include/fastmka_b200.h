@@ -23,9 +23,10 @@
  *                            mka/layers/fastmka.py:82-96; mka/hf/attention.py:97-107)
  *   fmka_route_ema_blend_state  the same with the EMA state carried across calls
  *                           (extends session_memory.py:6-22, which restarts at zero)
- *   fmka_route_ema_blend_kv the same for two levels on x [Wk ; Wv]^T, writing K/V
- *                           (the blend and k/v_proj of fastmka.py:94-99 and
- *                            hf/attention.py:105-119 in the commuted order)
+ *   fmka_route_ema_blend_kv the same on y = x [Wk ; Wv]^T (and y3 = L3 [Wk ; Wv]^T
+ *                           for three levels), writing K/V (the blend and
+ *                           k/v_proj of fastmka.py:94-99 and hf/attention.py:105-119
+ *                           in the commuted order)
  *   fmka_kv_proj            k/v projection of the fused memory (+ RoPE on k)
  *                           (mka/layers/fastmka.py:98-99; mka/hf/attention.py:110-119)
  *   fmka_attn_fwd_prefill   causal attention: fastmka_attn (mka/cuda/ops.py:73,
