@@ -17,13 +17,17 @@ e2e     = the same through the module API with the input copied from pinned host
           memory and the layer output copied back, every step
 roofline: the attention kernel (tensor-bound, algorithmic FLOPs 4*B*Hq*Dh*T(T+1)/2)
           timed with CUDA events inside the timed steps against the measured
-          sustained bf16 peak; decode: the split-KV kernel's K/V bytes against the
-          measured HBM copy bandwidth
+          burst bf16 peak (a ~2 ms kernel inside a ms-scale step, not a
+          seconds-long loop); decode: the split-KV kernel's K/V bytes against the
+          measured HBM copy bandwidth. Kernel times also appear in SM cycles
+          (ms x the median SM clock sampled during the run)
 Multi-GPU (torchrun): weak scaling by batch: every rank runs its own 4 sequences
 (units = (sequence, kv head) pairs, whole sequences per rank), no collective in
 the data path; the step time is the max over ranks.
 --impl reference: the reference's CPU algorithm (the CPU oracle restating
-FastLM/MKA's FastMKA forward op for op) on the host cores, one sequence per step.
+FastLM/MKA's FastMKA forward op for op) on the host cores, one whole 8192-token
+sequence of the prefill configuration per step (tokens/s of a sequence does not
+depend on the batch on the CPU, which runs the sequences one after another).
 """
 from __future__ import annotations
 
@@ -34,6 +38,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import torch
@@ -45,7 +50,7 @@ sys.path.insert(0, ROOT)
 PREFILL = dict(B=4, T=8192, D=3584, H=28, HKV=4, R=512, L=2, theta=1.0e6, bias=True)
 DECODE = dict(B=64, TK=32768, D=4096, H=32, HKV=8, R=2048, L=2, theta=5.0e5, bias=False)
 LONG = dict(B=2, T=32768, D=3584, H=28, HKV=4, R=512, L=3, theta=1.0e6, bias=True)
-CPU_SAMPLE_T = 2048  # CPU sample: the first 2048 tokens of one prefill sequence
+CPU_SEQ_T = PREFILL["T"]  # the CPU arms run one whole prefill sequence per step
 
 
 def _peaks():
@@ -112,7 +117,8 @@ class ClockSampler:
     def __init__(self, device_index):
         self.idx = device_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{device_index}.csv")
+        out_dir = os.environ.get("FMKA_BENCH_CLOCKS_DIR") or tempfile.gettempdir()
+        self.path = os.path.join(out_dir, f"fmka_clocks_rank{device_index}_{os.getpid()}.csv")
 
     def start(self):
         try:
@@ -308,9 +314,10 @@ def bench_prefill(args, dist, rank, world, device, peaks):
         "ms": ms, "tok_s": tokens / (ms * 1e-3), "e2e_tok_s": tokens / (e2e_ms * 1e-3), "e2e_ms": e2e_ms,
         "h2d": x.numel() * 2, "d2h": x.numel() * 2, "stages_ms": st,
         "roofline": {"bound": "tensor", "kernel": "attn_prefill", "achieved": round(achieved, 1),
-                     "peak": peaks["bf16_sust"], "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_sust"], 4),
-                     "peak_kind": f"{peaks['src']} sustained bf16", "algorithmic_tflop_per_launch": flops / 1e12,
-                     "launch_ms": attn_ms, "traffic": _traffic("attn_prefill")},
+                     "peak": peaks["bf16"], "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16"], 4),
+                     "peak_kind": f"{peaks['src']} burst bf16 (a ~2 ms kernel inside a ms-scale step)",
+                     "algorithmic_tflop_per_launch": flops / 1e12, "launch_ms": attn_ms,
+                     "traffic": _traffic("attn_prefill")},
         "layer": layer, "x": x, "pe": pe,
     }
 
@@ -369,7 +376,9 @@ def bench_long_context(args, dist, rank, world, device, peaks):
     B, T, D = c["B"], c["T"], c["D"]
     layer = build_layer(c, device, seed=2)
     groups = make_groups(B, c["HKV"], world) if dist is not None else {}
-    sh = HeadShardedFastMKA(layer, B, rank, world, groups, transport=args.exchange)
+    # the step stays asynchronous; the status word (peer timeouts included) is read once after the
+    # timed steps and reported as device_status
+    sh = HeadShardedFastMKA(layer, B, rank, world, groups, transport=args.exchange, check_peer_status=False)
     b0, b1 = sh.plan.batch
     g = torch.Generator(device=device).manual_seed(3000)
     x = (torch.randn(B, T, D, generator=g, device=device) / math.sqrt(D)).to(torch.bfloat16)[b0:b1].contiguous()
@@ -456,19 +465,24 @@ def _oracle_params(layer):
 
 
 def cpu_reference_step(p, x_cpu, cos, sin):
+    """One forward of the reference algorithm on the CPU (out, k/v, gate; the
+    reference computes no log-sum-exp, so neither does the timed step)."""
     from oracle import fastmka_oracle as orc
 
     with torch.no_grad():
-        orc.hf_fastmka_forward(x_cpu, p, PREFILL["H"], PREFILL["HKV"], False, 0.9, "silu", cos=cos, sin=sin)
+        orc.hf_fastmka_forward(x_cpu, p, PREFILL["H"], PREFILL["HKV"], False, 0.9, "silu", cos=cos, sin=sin,
+                               with_lse=False)
 
 
-def cpu_sample_inputs(seed=0):
-    """One cfg sequence prefix on the CPU: x [1, CPU_SAMPLE_T, D] fp32 and RoPE tables."""
+def cpu_sample_inputs(seed=0, t=None):
+    """One whole prefill sequence on the CPU: x [1, T, D] fp32 (T = CPU_SEQ_T by
+    default) and its RoPE tables."""
     c = PREFILL
+    t = t or CPU_SEQ_T
     g = torch.Generator().manual_seed(seed)
-    x = torch.randn(1, CPU_SAMPLE_T, c["D"], generator=g) / math.sqrt(c["D"])
+    x = torch.randn(1, t, c["D"], generator=g) / math.sqrt(c["D"])
     rot = _Rotary(c["theta"])
-    cos, sin = rot.cos_sin(torch.arange(CPU_SAMPLE_T), "cpu")
+    cos, sin = rot.cos_sin(torch.arange(t), "cpu")
     return x, cos[:, None], sin[:, None]
 
 
@@ -481,16 +495,18 @@ def cpu_params_random(seed=0):
             "bv": r(HKV * 128), "wo": r(D, H * 128), "r1w": r(R, D), "r1b": r(R), "r2w": r(2, R), "r2b": r(2)}
 
 
-def measure_cpu(p, steps=1):
+def measure_cpu(p, steps=1, warmup=1):
     torch.set_num_threads(os.cpu_count() or 1)
     x, cos, sin = cpu_sample_inputs()
+    for _ in range(warmup):
+        cpu_reference_step(p, x, cos, sin)
     t0 = time.perf_counter()
     for _ in range(steps):
         cpu_reference_step(p, x, cos, sin)
     dt = (time.perf_counter() - t0) / steps
-    return {"value": CPU_SAMPLE_T / dt, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"reference FastMKA forward (CPU oracle, fp32) on one sequence prefix: batch 1, "
-                      f"seq {CPU_SAMPLE_T} of the prefill config; {dt:.2f} s per step"}
+    return {"value": CPU_SEQ_T / dt, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"reference FastMKA forward (CPU oracle, fp32) on one whole sequence of the prefill "
+                      f"config (batch 1, seq {CPU_SEQ_T}); {dt:.2f} s per sequence after {warmup} warm-up"}
 
 
 def run_reference(args):
@@ -506,14 +522,14 @@ def run_reference(args):
     for _ in range(args.steps):
         cpu_reference_step(p, x, cos, sin)
     dt = (time.perf_counter() - t0) / args.steps
-    v = CPU_SAMPLE_T / dt
+    v = CPU_SEQ_T / dt
     cores = torch.get_num_threads()
     sample = (f"reference FastMKA forward (CPU oracle restating FastLM/MKA op for op, fp32, {cores} threads) on "
-              f"one sequence prefix per step: batch 1, seq {CPU_SAMPLE_T} of the prefill config")
+              f"one whole sequence per step: batch 1, seq {CPU_SEQ_T} of the prefill config")
     line = {"metric": "FastMKA prefill tokens/s (Qwen-7B-like layer, B200)", "value": v, "unit": "tokens/s",
-            "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "impl": "reference", "n_gpus": 0, "host_threads": cores, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic", "config": _config(args),
+            "dtype": "f32", "data": "synthetic", "config": _ref_config(cores),
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -596,6 +612,16 @@ def run_kernel_only(args):
     torch.cuda.synchronize()
     print(json.dumps({"only": args.only, "launches": n, "ms_per_launch": e0.elapsed_time(e1) / max(args.steps, 1),
                       "device_status": ops.device_status()}))
+
+
+def _ref_config(threads):
+    """What the CPU arm runs: one whole sequence of the prefill layer per step."""
+    c = PREFILL
+    return {"workload": f"FastMKA attention layer prefill, Qwen-7B-like: batch 1 (one whole sequence of the "
+                        f"prefill configuration per step), seq {CPU_SEQ_T}, d_model {c['D']}, {c['H']}/{c['HKV']} "
+                        f"heads, head_dim 128, L1+L2, router {c['D']}->{c['R']}->2, RoPE",
+            "global_batch": 1, "seq_len": CPU_SEQ_T, "parallelism": f"host CPU, {threads} threads",
+            "l2": "not applicable (CPU)"}
 
 
 def _config(args):
@@ -731,6 +757,10 @@ def main():
         except ValueError as e:
             lc = {"skipped": str(e)}
     clocks = sampler.stop()
+    mhz = clocks["sm_mhz"] if clocks else None
+
+    def mcycles(ms):  # kernel time in millions of SM cycles at the run's median clock
+        return None if mhz is None or ms is None else round(ms * mhz * 1e-3, 4)
     model = None
     if not args.no_model:
         if world == 1:
@@ -756,10 +786,11 @@ def main():
             "e2e": {"value": pre["e2e_tok_s"], "unit": "tokens/s", "h2d_bytes_per_step": pre["h2d"],
                     "d2h_bytes_per_step": pre["d2h"], "ms_per_step": pre["e2e_ms"],
                     "pipeline": "per sequence: upload of sequence u+1 and download of u-1 overlap the forward of u (3 streams)"},
-            "roofline": pre["roofline"],
+            "roofline": dict(pre["roofline"], launch_mcycles=mcycles(pre["roofline"]["launch_ms"])),
             "cpu_baseline": cpu,
             "gpu_launches": launches_per_step * args.steps,
             "stages_ms": {k: round(v, 4) for k, v in pre["stages_ms"].items()},
+            "stages_mcycles": {k: mcycles(v) for k, v in pre["stages_ms"].items()},
             "clocks": clocks,
             "device_status": status,
         }
@@ -769,11 +800,14 @@ def main():
                 "metric": "FastMKA decode tokens/s (Llama-3-8B-like layer, batch 64, 32768 cached)",
                 "value": dec["tok_s"], "unit": "tokens/s", "ms_per_step": dec["ms"], "roofline": dec["roofline"],
                 "stages_ms": {k: round(v, 4) for k, v in dec["stages_ms"].items()},
+                "stages_mcycles": {k: mcycles(v) for k, v in dec["stages_ms"].items()},
                 "config": {"batch_per_gpu": d["B"], "cache_len": d["TK"], "d_model": d["D"],
                            "heads": f"{d['H']}/{d['HKV']}"},
                 "gpu_launches": launches_per_step * args.steps,
             }
         if lc is not None:
+            if "roofline" in lc:
+                lc["roofline"]["launch_mcycles"] = mcycles(lc["roofline"]["launch_ms"])
             line["long_context"] = lc
         if model is not None:
             line["model"] = model

@@ -160,8 +160,10 @@ FMKA_API int fmka_route_ema_blend(const void* x, int64_t x_sb, int64_t x_st, con
  * every GPU that loads the library, so shapes whose
  * fmka_route_ema_blend_workspace_size() exceeds that are rejected with
  * FMKA_ERR_UNSUPPORTED. The first call on a device looks up the array's device
- * address (make it before any stream capture). All calls share the array:
- * calls that overlap on the GPU race. */
+ * address (make it before any stream capture) and keeps it for the life of the
+ * process: after a cudaDeviceReset of that device, unload and reload the library
+ * before calling this again. All calls share the array: calls that overlap on
+ * the GPU race. */
 FMKA_API int fmka_route_ema_blend_noalloc(const void* x, int64_t x_sb, int64_t x_st, const float* logits,
                                           const float* b2, const float* gate, int L, const void* l3, int64_t l3_sb,
                                           int64_t l3_st, int T3, float beta, int B, int T, int D, void* h,

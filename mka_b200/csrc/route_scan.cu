@@ -607,7 +607,9 @@ int launch_route_ema_blend_kv(const __nv_bfloat16* y, int64_t y_sb, int64_t y_st
 // In host code `g_route_scan_scratch` only names a host-side stand-in for the
 // symbol; the device address comes from cudaGetSymbolAddress, once per device,
 // with that device current (the first call on a device does it, so make that
-// first call before any stream capture). Every call shares the array and it
+// first call before any stream capture). The address is kept for the life of
+// the process; a cudaDeviceReset of that device invalidates it, so such a
+// caller unloads and reloads the library. Every call shares the array and it
 // keeps the previous call's contents: the flag region is cleared by a memset on
 // the calling stream before each launch, and calls that overlap on the GPU (on
 // different streams) race on the array.

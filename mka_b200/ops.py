@@ -22,6 +22,11 @@ from . import _lib
 HEAD_DIM = 128
 ACT_SILU = 0
 ACT_GELU = 1
+# bits of the device status word (FMKA_STATUS_* in include/fastmka_b200.h)
+STATUS_WAIT_TIMEOUT = 1
+STATUS_LOOKBACK_TIMEOUT = 2
+STATUS_BAD_LAUNCH = 4
+STATUS_PEER_TIMEOUT = 8
 
 
 # ------------------------------------------------------------------ helpers --
@@ -469,7 +474,9 @@ def _to_bf16(t: torch.Tensor) -> torch.Tensor:
 
 def fastmka_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True) -> torch.Tensor:
     """Drop-in for mka.cuda.ops.fastmka_attn (ops.py:73-77): causal attention with
-    offset Tk - Tq, output [B, H, Tq, D] in q's dtype. Adds GQA and bf16; D == 128."""
+    offset Tk - Tq, output [B, H, Tq, D] in q's dtype. Adds GQA and bf16; D == 128.
+    As in the reference kernel (fastmka_attn.cu:95,126-127), with causal and
+    Tq > Tk the first Tq - Tk queries see no key and their rows are zero."""
     _check_cuda(q, k, v)
     if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
         raise RuntimeError("q/k/v must be 4D")
@@ -481,11 +488,18 @@ def fastmka_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool
         raise RuntimeError(f"unsupported dtype {q.dtype}")
     qb, kb, vb = _to_bf16(q), _to_bf16(k), _to_bf16(v)
     B, H, Tq, D = q.shape
+    Tk = k.size(2)
     out = torch.empty((B, H, Tq, D), dtype=torch.bfloat16, device=q.device)
-    if Tq == 1 and causal:
-        attn_decode(qb, kb, vb, out=out.permute(0, 2, 1, 3), want_lse=False)
+    blind = Tq - Tk if causal and Tq > Tk else 0  # queries before the first key
+    if blind:
+        out[:, :, :blind].zero_()
+        qb, out_seen = qb[:, :, blind:], out[:, :, blind:]
     else:
-        attn_prefill(qb, kb, vb, causal=causal, out=out.permute(0, 2, 1, 3), want_lse=False)
+        out_seen = out
+    if qb.size(2) == 1 and causal:
+        attn_decode(qb, kb, vb, out=out_seen.permute(0, 2, 1, 3), want_lse=False)
+    else:
+        attn_prefill(qb, kb, vb, causal=causal, out=out_seen.permute(0, 2, 1, 3), want_lse=False)
     return out if q.dtype == torch.bfloat16 else out.to(q.dtype)
 
 
@@ -498,9 +512,19 @@ def fused_route_mka_attn(q: torch.Tensor, l1: torch.Tensor, l2: torch.Tensor, l3
         raise RuntimeError("q must be [B,H,T,Dh]")
     if l1.dim() != 3 or l2.dim() != 3 or l3.dim() != 3:
         raise RuntimeError("l1/l2/l3 must be [B,T,D]")
+    if lam.dim() != 3:
+        raise RuntimeError("lam must be [B,T,L]")
+    if wk.dim() != 2 or wv.dim() != 2:
+        raise RuntimeError("wk/wv must be [D,D]")
     B, H, T, Dh = q.shape
     D = l1.shape[2]
     L = lam.shape[2]
+    if l1.shape != l2.shape or l1.shape != l3.shape:
+        raise RuntimeError("l1/l2/l3 shapes must match")
+    if l1.shape[0] != B or l1.shape[1] != T:
+        raise RuntimeError("l1 batch/seq must match q")
+    if lam.shape[0] != B or lam.shape[1] != T:
+        raise RuntimeError("lam batch/seq must match q")
     if L not in (2, 3):
         raise RuntimeError("lam last dim must be 2 or 3")
     if H * Dh != D or wk.shape != (D, D) or wv.shape != (D, D):

@@ -105,14 +105,23 @@ class HeadShardedFastMKA(nn.Module):
     it to keep it longer). The peer exchange needs T divisible by the group
     size; other lengths take the NCCL all-gather. Call `close()` on every rank
     before the process group is destroyed.
+
+    A peer barrier that waits longer than its 2 s limit (a rank of the group
+    never arrived) returns with FMKA_STATUS_PEER_TIMEOUT set in the device
+    status word, and the step's output is then incomplete. With
+    `check_peer_status` (the default) every peer-exchange forward reads the
+    status word once at its end (one stream synchronisation) and raises
+    PeerExchangeError; a caller that polls `ops.device_status()` itself can turn
+    the check off to keep the stream asynchronous.
     """
 
     def __init__(self, layer: nn.Module, batch: int, rank: int, world_size: int, groups: Optional[dict] = None,
-                 transport: str = "peer"):
+                 transport: str = "peer", check_peer_status: bool = True):
         super().__init__()
         if transport not in ("peer", "nccl"):
             raise ValueError("transport must be 'peer' or 'nccl'")
         self.transport = transport
+        self.check_peer_status = check_peer_status
         self._region: Optional[PeerRegion] = None
         self._region_key = None
         self.layer = layer
@@ -190,6 +199,8 @@ class HeadShardedFastMKA(nn.Module):
         # o_proj on this rank's rows, each written into every rank's output
         ops.gemm_kblocked_scatter(gathered, W.w_o, W.b_o, [p + pl.out_off for p in reg.ptrs], pl.gemm_row0, D)
         reg.barrier(stream)  # every rank's o_proj rows have landed here
+        if self.check_peer_status:
+            raise_on_peer_timeout()
         return bf16_view(reg.local + pl.out_off, (T, D), x.device).view(1, T, D)
 
     def close(self) -> None:
@@ -198,6 +209,18 @@ class HeadShardedFastMKA(nn.Module):
             self._region.close()
             self._region = None
             self._region_key = None
+
+
+class PeerExchangeError(RuntimeError):
+    """A cross-GPU barrier of the peer exchange ran out of time."""
+
+
+def raise_on_peer_timeout() -> None:
+    """Reads the device status word (without clearing it) and raises
+    PeerExchangeError when a peer barrier has timed out since it was last cleared."""
+    if ops.device_status(clear=False) & ops.STATUS_PEER_TIMEOUT:
+        raise PeerExchangeError("head-sharded FastMKA: a peer barrier ran out of time (a rank of the sequence "
+                                "group did not arrive within 2 s); this step's layer output is incomplete")
 
 
 def fastmka_forward_heads(x: torch.Tensor, W: PreparedWeights, hq: int, hkv: int, beta: float, use_l3: bool,

@@ -112,25 +112,67 @@ def attention(q: Tensor, k: Tensor, v: Tensor, use_sdpa: bool) -> Tensor:
 
 def attention_lse(q: Tensor, k: Tensor) -> Tensor:
     """Log-sum-exp over keys of the scaled, causally masked scores (bottom-right
-    alignment), the second output of the flash kernel: [B, Hq, Tq]."""
+    alignment), the second output of the flash kernel: [B, Hq, Tq]. Computed one
+    query head at a time so that long sequences stay within host memory."""
     g = q.size(1) // k.size(1)
-    kk = repeat_kv(k, g)
-    t, t_tot = q.size(2), kk.size(2)
-    s = torch.matmul(q.float(), kk.float().transpose(-1, -2)) / math.sqrt(q.size(-1))
-    q_pos = torch.arange(t_tot - t, t_tot).view(1, 1, t, 1)
-    k_pos = torch.arange(t_tot).view(1, 1, 1, t_tot)
-    s = s.masked_fill(k_pos > q_pos, float("-inf"))
-    return torch.logsumexp(s, dim=-1)
+    t, t_tot = q.size(2), k.size(2)
+    q_pos = torch.arange(t_tot - t, t_tot).view(1, t, 1)
+    k_pos = torch.arange(t_tot).view(1, 1, t_tot)
+    masked = k_pos > q_pos
+    out = torch.empty(q.shape[:3], dtype=torch.float32)
+    for h in range(q.size(1)):
+        s = torch.matmul(q[:, h].float(), k[:, h // g].float().transpose(-1, -2)) / math.sqrt(q.size(-1))
+        out[:, h] = torch.logsumexp(s.masked_fill(masked, float("-inf")), dim=-1)
+    return out
+
+
+# ------------------------------------------------------- low-level op API --
+def fastmka_attn_op(q: Tensor, k: Tensor, v: Tensor, causal: bool = True) -> Tensor:
+    """The reference's fastmka_attn op (mka/cuda/fastmka_attn.cu:51-131, bound at
+    mka/cuda/ops.py:73-77): q [B,H,Tq,D], k/v [B,H,Tk,D]; query tq attends keys
+    0 .. min(Tk-1, tq + Tk - Tq) when causal, all keys otherwise; a query with no
+    key to attend (Tq > Tk) gets zeros (inv_l = 0 at :126-127). Scale 1/sqrt(D).
+    A k/v with fewer heads than q is broadcast by head group (the B200 op's GQA
+    extension; the reference requires equal head counts)."""
+    g = q.size(1) // k.size(1)
+    qf, kf, vf = q.float(), repeat_kv(k.float(), g), repeat_kv(v.float(), g)
+    tq, tk = qf.size(2), kf.size(2)
+    s = torch.matmul(qf, kf.transpose(-1, -2)) / math.sqrt(qf.size(-1))
+    if causal:
+        q_pos = torch.arange(tk - tq, tk).view(1, 1, tq, 1)
+        k_pos = torch.arange(tk).view(1, 1, 1, tk)
+        s = s.masked_fill(k_pos > q_pos, float("-inf"))
+    p = torch.softmax(s, dim=-1).nan_to_num(0.0)  # rows with every key masked -> zeros
+    return torch.matmul(p, vf)
+
+
+def fused_route_mka_op(q: Tensor, l1: Tensor, l2: Tensor, l3: Tensor, lam: Tensor, wk: Tensor,
+                       wv: Tensor) -> Tensor:
+    """The reference's fused_route_mka op (mka/cuda/fused_route_mka.cu:23-102,
+    bound at mka/cuda/ops.py:47-70): per token fused = lam0 l1 + lam1 l2 (+ lam2 l3
+    when lam has 3 levels), k = fused wk^T and v = fused wv^T split into H heads of
+    Dh = D / H, then causal attention of q [B,H,T,Dh] over them (offset 0)."""
+    b, h, t, dh = q.shape
+    d = l1.size(2)
+    n_levels = lam.size(2)
+    fused = lam[..., 0:1].float() * l1.float() + lam[..., 1:2].float() * l2.float()
+    if n_levels > 2:
+        fused = fused + lam[..., 2:3].float() * l3.float()
+    k = F.linear(fused, wk.float()).view(b, t, h, dh).transpose(1, 2)
+    v = F.linear(fused, wv.float()).view(b, t, h, dh).transpose(1, 2)
+    assert h * dh == d
+    return fastmka_attn_op(q, k, v, causal=True)
 
 
 # ------------------------------------------------------------- full forwards --
 def fastmka_forward(x: Tensor, p: Dict[str, Tensor], num_heads: int, use_l3: bool, beta: float, act: str,
                     l3_memory: Optional[Tensor] = None, kv_cache_k: Optional[Tensor] = None,
-                    kv_cache_v: Optional[Tensor] = None) -> Dict[str, Tensor]:
+                    kv_cache_v: Optional[Tensor] = None, with_lse: bool = True) -> Dict[str, Tensor]:
     """FastMKAAttention.forward (mka/layers/fastmka.py:71-177), MHA, no biases.
 
     p: wq, wk, wv, wo [D, D]; r1w [R, D], r1b [R], r2w [L, R], r2b [L].
-    Returns out, k_tot, v_tot, lam and lse.
+    Returns out, k_tot, v_tot, lam and (with_lse) lse, which the reference
+    module does not compute: a timed run of the reference algorithm leaves it out.
     """
     b, t, d = x.shape
     dh = d // num_heads
@@ -152,13 +194,14 @@ def fastmka_forward(x: Tensor, p: Dict[str, Tensor], num_heads: int, use_l3: boo
     v_tot = torch.cat([kv_cache_v, v_new], 2) if cached else v_new
     o = attention(qh, k_tot, v_tot, use_sdpa=not cached)
     out = F.linear(o.transpose(1, 2).contiguous().view(b, t, d), p["wo"])
-    return {"out": out, "k_tot": k_tot, "v_tot": v_tot, "lam": lam, "lse": attention_lse(qh, k_tot)}
+    return {"out": out, "k_tot": k_tot, "v_tot": v_tot, "lam": lam,
+            "lse": attention_lse(qh, k_tot) if with_lse else None}
 
 
 def hf_fastmka_forward(h: Tensor, p: Dict[str, Tensor], num_heads: int, num_kv_heads: int, use_l3: bool,
                        beta: float, act: str, past: Optional[Tuple[Tensor, Tensor]] = None,
                        cos: Optional[Tensor] = None, sin: Optional[Tensor] = None,
-                       l3_memory: Optional[Tensor] = None) -> Dict[str, Tensor]:
+                       l3_memory: Optional[Tensor] = None, with_lse: bool = True) -> Dict[str, Tensor]:
     """HFFastMKAAttention.forward (mka/hf/attention.py:82-199): GQA, optional
     q/k/v/o biases (bq, bk, bv, bo in p), RoPE when cos/sin are given
     (:113-119), tuple cache concat (:121-124), present = post-RoPE (k, v).
@@ -166,6 +209,8 @@ def hf_fastmka_forward(h: Tensor, p: Dict[str, Tensor], num_heads: int, num_kv_h
     l3_memory: the per-position L3 of the cfg-3 workload, composed from the
     reference's own functions as in fastmka.py:84-89; the HF wrapper itself
     always blends zeros (hf/attention.py:100-102), which is l3_memory=None.
+    with_lse: also return the attention log-sum-exp (not part of the reference
+    forward; a timed run of the reference algorithm leaves it out).
     """
     b, t, d = h.shape
     dh = d // num_heads
@@ -187,4 +232,4 @@ def hf_fastmka_forward(h: Tensor, p: Dict[str, Tensor], num_heads: int, num_kv_h
     g = num_heads // num_kv_heads
     o = attention(qs, repeat_kv(ks, g), repeat_kv(vs, g), use_sdpa=past is None)
     out = F.linear(o.transpose(1, 2).contiguous().view(b, t, d), p["wo"], p.get("bo"))
-    return {"out": out, "k": ks, "v": vs, "lam": lam, "lse": attention_lse(qs, ks)}
+    return {"out": out, "k": ks, "v": vs, "lam": lam, "lse": attention_lse(qs, ks) if with_lse else None}

@@ -1,6 +1,7 @@
 """Generates the golden fixtures by running the FastLM/MKA reference modules.
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <reference checkout>
+    (or set FMKA_REFERENCE_DIR to the checkout and omit --ref)
 
 Needs the reference package on disk (it is not on the GPU box: the fixtures are
 committed). Every input is rounded to bf16-representable values before the
@@ -228,7 +229,9 @@ def make_ema_cases(mka) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    env = os.environ.get("FMKA_REFERENCE_DIR")
+    ap.add_argument("--ref", default=env, required=env is None,
+                    help="the FastLM/MKA checkout (the directory holding the mka package)")
     a = ap.parse_args()
     sys.path.insert(0, a.ref)
     import mka  # noqa: F401  (the reference package)

@@ -16,7 +16,9 @@ def test_reference_arm_prints_one_contract_line():
     lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
     assert len(lines) == 1
     d = json.loads(lines[0])
-    assert d["impl"] == "reference" and d["n_gpus"] == 1 and d["steps"] == 1
+    assert d["impl"] == "reference" and d["n_gpus"] == 0 and d["steps"] == 1
+    # the line names what ran: one whole sequence of the prefill configuration
+    assert d["config"]["global_batch"] == 1 and d["config"]["seq_len"] == 8192
     assert d["metric"].startswith("FastMKA prefill tokens/s") and d["unit"] == "tokens/s"
     assert d["higher_is_better"] is True and d["value"] > 0
     assert d["e2e"]["value"] == d["value"] and d["e2e"]["unit"] == d["unit"]

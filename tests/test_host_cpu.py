@@ -214,3 +214,26 @@ def test_static_kv_cache_bookkeeping():
     s_in2, s_out2 = c.ema_buffers(a, 256, "cpu")
     assert s_in2.data_ptr() == s_out.data_ptr() and s_out2.data_ptr() == s_in.data_ptr()
     assert bool((s_in2 == 1.0).all())
+
+
+def test_peer_timeout_in_status_word_raises(monkeypatch):
+    """A peer barrier that ran out of time leaves FMKA_STATUS_PEER_TIMEOUT in the
+    device status word; the head-sharded layer's check turns it into an error
+    (the status read is replaced by a fake, so no GPU is needed)."""
+    from mka_b200 import ops, sharded
+
+    seen = []
+
+    def fake_status(clear=True):
+        seen.append(clear)
+        return fake_status.word
+
+    monkeypatch.setattr(ops, "device_status", fake_status)
+    fake_status.word = 0
+    sharded.raise_on_peer_timeout()
+    fake_status.word = ops.STATUS_LOOKBACK_TIMEOUT  # other bits are not this check's business
+    sharded.raise_on_peer_timeout()
+    fake_status.word = ops.STATUS_PEER_TIMEOUT | ops.STATUS_WAIT_TIMEOUT
+    with pytest.raises(sharded.PeerExchangeError, match="peer barrier"):
+        sharded.raise_on_peer_timeout()
+    assert seen == [False, False, False]  # the word is left for the caller's own poll

@@ -115,3 +115,53 @@ def test_oracle_hf_matches_reference(name):
     _close(r["v"], c["v"])
     _close(r["lam"], c["lam"])
     _close(r["lse"], c["lse"])
+
+
+def _online_softmax_rows(q, k, v, causal):
+    """Row-by-row restatement of the reference kernel's loop (fastmka_attn.cu:95-129):
+    running max m, sum l and accumulator rescaled per key; l == 0 gives zeros."""
+    b_, h_, tq, d = q.shape
+    tk = k.shape[2]
+    out = torch.zeros(b_, h_, tq, d, dtype=torch.float64)
+    for b in range(b_):
+        for h in range(h_):
+            for i in range(tq):
+                m, l, acc = float("-inf"), 0.0, torch.zeros(d, dtype=torch.float64)
+                limit = min(tk - 1, i + tk - tq) if causal else tk - 1
+                for j in range(limit + 1):
+                    s = float(q[b, h, i].double() @ k[b, h, j].double()) / d ** 0.5
+                    m_new = max(m, s)
+                    alpha = 0.0 if m == float("-inf") else float(torch.tensor(m - m_new).exp())
+                    beta = float(torch.tensor(s - m_new).exp())
+                    l = l * alpha + beta
+                    acc = acc * alpha + beta * v[b, h, j].double()
+                    m = m_new
+                out[b, h, i] = acc / l if l > 0 else acc * 0
+    return out
+
+
+@pytest.mark.parametrize("tq,tk,causal", [(6, 6, True), (4, 9, True), (7, 3, True), (5, 8, False)])
+def test_oracle_fastmka_attn_op_matches_kernel_loop(tq, tk, causal):
+    """The op oracle equals the reference kernel's per-row online softmax, including
+    the causal offset Tk - Tq and the zero rows of queries with no visible key."""
+    g = torch.Generator().manual_seed(tq * 10 + tk)
+    q, k, v = (torch.randn(1, 2, n, 8, generator=g) for n in (tq, tk, tk))
+    _close(orc.fastmka_attn_op(q, k, v, causal), _online_softmax_rows(q, k, v, causal).float(), 1e-5)
+
+
+@pytest.mark.parametrize("name", ["fastmka_mha_gelu", "fastmka_mha_l3_pad"])
+def test_oracle_fused_route_op_matches_reference_module(name):
+    """With H * Dh == D the reference's fused op is the module's blend, K/V
+    projection and attention (mka/cuda/ops.py:55 'matches FastMKA math'): feeding it
+    the module's own levels and gate, then projecting with wo, gives the golden out."""
+    import torch.nn.functional as F
+
+    c = golden_io.load(name)
+    p = _fastmka_params(c)
+    x = c["x"]
+    b, t, d = x.shape
+    h = int(c["heads"])
+    l3 = orc.repeat_retrieval_to_length(c["l3"], t) if "l3" in c else torch.zeros_like(x)
+    q = F.linear(x, p["wq"]).view(b, t, h, d // h).transpose(1, 2)
+    o = orc.fused_route_mka_op(q, x, orc.causal_prefix_ema(x, float(c["beta"])), l3, c["lam"], p["wk"], p["wv"])
+    _close(F.linear(o.transpose(1, 2).reshape(b, t, d), p["wo"]), c["out"])

@@ -5,7 +5,12 @@ the layer output, k, v and the attention log-sum-exp; the gate lambda within
 2e-2 absolute.
   * golden fixtures: the reference modules' own outputs (tests/golden)
   * the single-layer fp32 configuration at full size against the CPU oracle
-  * the Qwen-7B-like prefill layer at full size (batch 4, seq 8192, 28/4 heads)
+  * the Qwen-7B-like prefill layer on one whole sequence of 8192 tokens against
+    the CPU oracle (out, k, v, gate, LSE)
+  * the long-context layer (three levels, per-position L3 memory, GQA, RoPE) at
+    full width on one whole sequence of 4096 tokens, and at a small width with
+    L3 memories that are truncated, padded and repeated
+  * the Qwen-7B-like prefill layer at the full batch (batch 4, seq 8192)
     through size-independent checks: exact softmax rows recomputed in fp32 for
     sampled queries, the EMA/blend recurrence for sampled channels, and the
     causal prefix property
@@ -309,3 +314,112 @@ def test_hf_decode_carried_ema_matches_whole_sequence_prefill():
         ref2 = orc.hf_fastmka_forward(x[:, T0:T0 + 1].float(), p, H, HKV, False, layer.ema_beta, "silu",
                                       past=(ref["k"], ref["v"]))
     assert nrel(out2, ref2["out"]) < TOL
+
+
+class _RopeTables:
+    """Stands in for an HF rotary module (its presence makes the wrapper apply
+    RoPE, hf/attention.py:113-119); cos/sin are passed as position_embeddings."""
+
+    def __init__(self, theta):
+        self.theta = theta
+
+    def tables(self, t):
+        inv = 1.0 / (self.theta ** (torch.arange(0, 128, 2, dtype=torch.float64) / 128))
+        ang = torch.arange(t, dtype=torch.float64)[:, None] * inv[None]
+        ang = torch.cat([ang, ang], -1)
+        return ang.cos().float()[None], ang.sin().float()[None]  # [1, T, 128]
+
+
+def _gqa_l3_layer(D, H, HKV, R, levels, seed, w_std, theta=1.0e6):
+    """A Qwen2-like attention (q/k/v bias, GQA, RoPE) wrapped by HFFastMKAAttention
+    with a router D -> R -> levels (SiLU); weights and biases N(0, w_std), fp32."""
+    from mka_b200 import HFFastMKAAttention
+
+    class _Attn(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.hidden_size, self.num_heads, self.num_key_value_heads = D, H, HKV
+            self.q_proj = nn.Linear(D, H * 128, bias=True)
+            self.k_proj = nn.Linear(D, HKV * 128, bias=True)
+            self.v_proj = nn.Linear(D, HKV * 128, bias=True)
+            self.o_proj = nn.Linear(H * 128, D, bias=False)
+            self.rotary_emb = _RopeTables(theta)
+
+    torch.manual_seed(seed)
+    layer = HFFastMKAAttention(_Attn(), use_l3=levels == 3)
+    layer.router = nn.Sequential(nn.Linear(D, R), nn.SiLU(), nn.Linear(R, levels))
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        for m in layer.modules():
+            if isinstance(m, nn.Linear):
+                m.weight.copy_(torch.randn(m.weight.shape, generator=g) * w_std)
+                if m.bias is not None:
+                    m.bias.copy_(torch.randn(m.bias.shape, generator=g) * w_std)
+    f = lambda t: None if t is None else t.detach().float().clone()  # noqa: E731
+    p = {"wq": f(layer.q_proj.weight), "bq": f(layer.q_proj.bias), "wk": f(layer.k_proj.weight),
+         "bk": f(layer.k_proj.bias), "wv": f(layer.v_proj.weight), "bv": f(layer.v_proj.bias),
+         "wo": f(layer.o_proj.weight), "r1w": f(layer.router[0].weight), "r1b": f(layer.router[0].bias),
+         "r2w": f(layer.router[2].weight), "r2b": f(layer.router[2].bias)}
+    return layer.cuda().eval(), p
+
+
+def _check_gqa_layer(layer, p, x, H, HKV, l3=None):
+    """The wrapper on the GPU against the oracle's HF forward (hf/attention.py:82-199,
+    with the per-position L3 level composed as in fastmka.py:84-89): out, the
+    present k/v, the gate and the attention log-sum-exp."""
+    B, T, D = x.shape
+    cos, sin = layer.rotary_emb.tables(T)
+    with torch.no_grad():
+        ref = orc.hf_fastmka_forward(x, p, H, HKV, l3 is not None, layer.ema_beta, "silu", cos=cos[:, None],
+                                     sin=sin[:, None], l3_memory=l3)
+    kw = {"position_embeddings": (cos.cuda(), sin.cuda()), "use_cache": True}
+    if l3 is not None:
+        kw["l3_memory"] = l3.cuda().bfloat16()
+    out, _, present, lse, lam = layer.forward_with_lse(x.cuda().bfloat16(), **kw)
+    errs = {"out": nrel(out, ref["out"]), "k": nrel(present[0], ref["k"]), "v": nrel(present[1], ref["v"]),
+            "lse": nrel(lse, ref["lse"]), "lam": (lam.float().cpu() - ref["lam"]).abs().max().item()}
+    from mka_b200 import ops
+
+    assert ops.device_status() == 0
+    assert all(e < TOL for e in errs.values()), errs
+    return errs
+
+
+@pytest.mark.parametrize("t3", ["same", "longer", "shorter", "one"])
+def test_hf_gqa_three_levels_per_position_l3(t3):
+    """Three levels with a per-position L3 memory on the GQA + RoPE wrapper (the
+    long-context configuration's layer at a small size): L3 of T rows, of more
+    rows than T (truncated), of fewer (padded with its last row) and of one row
+    (repeated), session_memory.py:25-39."""
+    B, T, D, H, HKV = 2, 200, 512, 4, 2
+    layer, p = _gqa_l3_layer(D, H, HKV, 256, 3, seed=21, w_std=0.05)
+    g = torch.Generator().manual_seed(22)
+    x = torch.randn(B, T, D, generator=g).bfloat16().float()
+    t3n = {"same": T, "longer": T + 40, "shorter": T - 30, "one": 1}[t3]
+    l3 = (torch.randn(B, t3n, D, generator=g) * 0.5).bfloat16().float()
+    _check_gqa_layer(layer, p, x, H, HKV, l3=l3)
+
+
+def test_long_context_layer_three_levels_full_width():
+    """The long-context configuration's layer at its full width on one whole
+    sequence: d_model 3584, 28/4 heads, q/k/v bias, RoPE theta 1e6, router
+    3584 -> 512 -> 3, weights N(0, 0.02), X ~ N(0,1)/sqrt(3584), L3 ~ N(0,1)*0.5
+    per position, seq 4096."""
+    D, H, HKV, T = 3584, 28, 4, 4096
+    layer, p = _gqa_l3_layer(D, H, HKV, 512, 3, seed=23, w_std=0.02)
+    g = torch.Generator().manual_seed(24)
+    x = (torch.randn(1, T, D, generator=g) / math.sqrt(D)).bfloat16().float()
+    l3 = (torch.randn(1, T, D, generator=g) * 0.5).bfloat16().float()
+    _check_gqa_layer(layer, p, x, H, HKV, l3=l3)
+
+
+def test_qwen_like_prefill_whole_sequence():
+    """The Qwen-7B-like prefill layer (d_model 3584, 28/4 heads, q/k/v bias, RoPE
+    theta 1e6, router 3584 -> 512 -> 2, weights N(0, 0.02), X ~ N(0,1)/sqrt(3584))
+    on one whole sequence of 8192 tokens: out, k, v, gate and LSE against the
+    oracle's fp32 forward of the same sequence."""
+    D, H, HKV, T = 3584, 28, 4, 8192
+    layer, p = _gqa_l3_layer(D, H, HKV, 512, 2, seed=25, w_std=0.02)
+    g = torch.Generator().manual_seed(26)
+    x = (torch.randn(1, T, D, generator=g) / math.sqrt(D)).bfloat16().float()
+    _check_gqa_layer(layer, p, x, H, HKV)

@@ -5,10 +5,11 @@ a serving runtime that reserved the whole GPU for its own pools, a real-time
 path that must not trigger cudaMalloc's implicit synchronisation, or a C
 program that links only this library. Its scratch is a fixed 4 MiB device array
 inside the library instead of a caller workspace. These tests call it through
-the C ABI and check it against the workspace entry point on two calls in a row
-(the array keeps the previous call's contents, so the second call checks that
-what must start at zero is cleared), and that shapes needing more scratch than
-the array holds are refused before anything is launched.
+the C ABI and check it against the workspace entry point and an fp32
+restatement of the gate, EMA and blend on two calls in a row (the array keeps
+the previous call's contents, so the second call checks that what must start at
+zero is cleared), and that shapes needing more scratch than the array holds are
+refused before anything is launched.
 
 This file is named to be collected last.
 """
@@ -47,6 +48,16 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls():
     logits = torch.randn(B * T, L, generator=g, device="cuda")
     b2 = torch.randn(L, generator=g, device="cuda")
     ref_h, ref_lam = ops.route_ema_blend(x, 0.9, logits=logits, b2=b2, levels=L, l3=l3)
+    # an fp32 restatement as well, so that a fault shared by both entry points shows:
+    # lam = softmax(logits + b2), L2 = EMA(x) from a zero state, h = lam0 x + lam1 L2 + lam2 L3
+    lam32 = torch.softmax(logits + b2, -1).view(B, T, L)
+    xf = x.float()
+    ema = torch.empty_like(xf)
+    st = torch.zeros(B, D, device="cuda")
+    for t in range(T):
+        st = 0.9 * st + 0.1 * xf[:, t]
+        ema[:, t] = st
+    h32 = lam32[..., 0:1] * xf + lam32[..., 1:2] * ema + lam32[..., 2:3] * l3.float()
     for _ in range(2):
         h = torch.full_like(x, float("nan"))
         lam = torch.full((B, T, L), float("nan"), device="cuda")
@@ -56,6 +67,9 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls():
         err = ((h.float() - ref_h.float()).abs().max() / ref_h.float().abs().max()).item()
         assert err < TOL
         assert (lam - ref_lam).abs().max().item() < 1e-6
+        err32 = ((h.float() - h32).abs().max() / h32.abs().max()).item()
+        assert err32 < TOL
+        assert (lam - lam32).abs().max().item() < 1e-5
     assert ops.device_status() == 0
 
 
