@@ -13,19 +13,26 @@
 //
 // Parallel scan. The EMA is a linear recurrence, so the state after a chunk is
 // the chunk's zero-state scan ("aggregate") plus beta^len times the state that
-// entered it; a chunk only needs its incoming state S_in to finish. Each CTA owns (batch row,
-// 256-channel slice, 64-token chunk). Eight warps each scan eight tokens with
-// 128-bit loads (lane = 8 channels); warp aggregates are combined in shared
-// memory; the chunk's incoming state comes from a decoupled look-back over
-// preceding chunks of the same (batch, slice): each CTA publishes its chunk
-// aggregate, then walks back over published aggregates until it finds a
-// published inclusive state. Chunk order comes from an atomic ticket, so a CTA
-// only ever waits on CTAs that started before it. Waits are bounded; a timeout
-// sets a status bit and the scan continues with a zero contribution. Three
-// CTAs share an SM so that one CTA's look-back latency is covered by the
-// others' loads (measured on the layer's K/V-mode scan, batch 4 x 8192 tokens:
-// 0.106 ms at three CTAs, 76 registers a thread, against 0.109 ms at four,
-// where the 64-register cap spills more, and 0.116 ms with 128-token chunks).
+// entered it; a chunk only needs its incoming state S_in to finish. Each CTA
+// owns (batch row, 256-channel slice, 64-token chunk). Eight warps each scan
+// eight tokens with 128-bit loads (lane = 8 channels); warp aggregates are
+// combined in shared memory (two float4 planes per row, conflict-free). The
+// chunk's incoming state comes from the preceding chunks of the same (batch,
+// slice):
+//   * short memory (beta^(64 k) < 2^-40 within k <= 32 chunks, e.g. beta = 0.9:
+//     k = 5): the weighted sum of the k preceding chunk aggregates, read by k
+//     warps in parallel. Older chunks weigh less than 2^-40 and are left out;
+//     no chunk waits on more than the aggregates of its k predecessors;
+//   * long memory: a decoupled look-back, each CTA publishing its aggregate,
+//     then walking back over published aggregates until it finds a published
+//     inclusive state.
+// Chunk order comes from an atomic ticket, so a CTA only ever waits on CTAs
+// that started before it. Waits are bounded; a timeout sets a status bit and the
+// scan continues with a zero contribution. Three CTAs share an SM so that one
+// CTA's waits are covered by the others' loads. Measured on the layer's K/V-mode
+// scan (batch 4 x 8192 tokens, 1024 channels): 0.121 ms with the [32][8]
+// shared-memory layout, whose eight-way bank conflicts kept the L1 pipe 74 %
+// busy, and 0.074 ms with the float4 planes.
 #include <mutex>
 
 #include "fmka_internal.h"
@@ -35,10 +42,13 @@ namespace fmka {
 
 namespace {
 
-constexpr int kChunkT = 64;   // tokens per CTA
+#ifndef FMKA_SCAN_WARPS
+#define FMKA_SCAN_WARPS 8
+#endif
+constexpr int kWarps = FMKA_SCAN_WARPS;
+constexpr int kTokPerWarp = 8;
+constexpr int kChunkT = kWarps * kTokPerWarp;  // tokens per CTA (64)
 constexpr int kSlice = 256;   // channels per CTA (32 lanes x 8)
-constexpr int kWarps = 8;
-constexpr int kTokPerWarp = kChunkT / kWarps;  // 8
 constexpr int kThreads = kWarps * 32;
 
 #ifndef FMKA_SCAN_MINB
@@ -59,7 +69,14 @@ struct ScanParams {
   const __nv_bfloat16* l3; // [B, T3, D] or null
   int64_t l3_sb, l3_st;
   int T3;
-  float beta, one_minus_beta, beta8, beta64;
+  float beta, one_minus_beta, beta8, beta_chunk;  // beta_chunk = beta^kChunkT
+  // Short-memory look-back: when beta^(kChunkT * lb_max) < 2^-40 (beta <= ~0.98
+  // at 64-token chunks), the state entering a chunk is the sum of the lb_max
+  // preceding chunk aggregates weighted by beta^(kChunkT k); older chunks weigh less than 2^-40 of
+  // the newest one, far below fp32 resolution, and are left out. Each chunk then
+  // waits only for the aggregates of its lb_max predecessors (no inclusive
+  // states, no chain). lb_max == 0: the full decoupled look-back.
+  int lb_max;
   int B, T, D;
   __nv_bfloat16* h;        // [B, T, D]
   int64_t h_sb, h_st;
@@ -104,6 +121,21 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
   f[5] = bf16hi_to_f32(u.z);
   f[6] = bf16lo_to_f32(u.w);
   f[7] = bf16hi_to_f32(u.w);
+}
+
+__device__ __forceinline__ float ipow(float b, int e);
+
+// A lane's 8 channels in shared memory as two float4 planes ([2][32] per row):
+// consecutive lanes hit consecutive 16-byte words, so a warp's access is
+// conflict-free (a [32][8] float layout would serialise it eight ways).
+__device__ __forceinline__ void put8(float4 (&row)[2][32], int lane, const float (&v)[8]) {
+  row[0][lane] = make_float4(v[0], v[1], v[2], v[3]);
+  row[1][lane] = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ void get8(const float4 (&row)[2][32], int lane, float (&v)[8]) {
+  const float4 a = row[0][lane], b = row[1][lane];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
 // Warp 0 of the CTA that owns (seq, chunk): publishes the chunk aggregate `a`
@@ -173,19 +205,58 @@ __device__ __forceinline__ void chunk_lookback(const ScanParams& p, int seq, int
         sin_[5] += mult * v1.y;
         sin_[6] += mult * v1.z;
         sin_[7] += mult * v1.w;
-        mult *= p.beta64;
+        mult *= p.beta_chunk;
       }
       if (l_inc < 32) break;
       base -= 32;
     }
     float inc[8];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) inc[c] = a[c] + p.beta64 * sin_[c];
+    for (int c = 0; c < 8; ++c) inc[c] = a[c] + p.beta_chunk * sin_[c];
     float4* dst = reinterpret_cast<float4*>(p.inc + rec * kSlice + lane * 8);
     __stcg(dst, make_float4(inc[0], inc[1], inc[2], inc[3]));
     __stcg(dst + 1, make_float4(inc[4], inc[5], inc[6], inc[7]));
     __syncwarp();
     if (lane == 0) st_release_u32(p.flags + rec, kFlagInc);
+  }
+}
+
+// Short-memory look-back, run by every warp: warp w adds the aggregates of
+// predecessor chunks chunk-1-k, k = w, w + kWarps, ... < lb_max, each weighted
+// by beta^(64 k), into part (this lane's 8 channels). Every lane polls the flag
+// (a broadcast load) so that each lane's own acquire orders its record reads.
+__device__ __forceinline__ void short_lookback(const ScanParams& p, int seq, int chunk, int warp, float (&part)[8]) {
+  const int lane = lane_id();
+  const uint32_t* seq_flags = p.flags + (int64_t)seq * p.nchunks;
+  const int64_t seq_rec = (int64_t)seq * p.nchunks;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) part[c] = 0.f;
+  for (int k = warp; k < p.lb_max; k += kWarps) {
+    const int pc = chunk - 1 - k;
+    if (pc < 0) break;
+    const uint64_t tstart = globaltimer_ns();
+    bool ok = true;
+    while (ld_acquire_u32(seq_flags + pc) == 0u) {
+      if (globaltimer_ns() - tstart > kWaitLimitNs) {
+        if (lane == 0) atomicOr(p.status, kStatusLookbackTimeout);
+        ok = false;  // give up: this predecessor counts as zero
+        break;
+      }
+      __nanosleep(32);
+    }
+    if (!ok) continue;
+    const float w = ipow(p.beta_chunk, k);
+    const float* src = p.agg + (seq_rec + pc) * kSlice + lane * 8;
+    const float4 v0 = __ldcg(reinterpret_cast<const float4*>(src));
+    const float4 v1 = __ldcg(reinterpret_cast<const float4*>(src) + 1);
+    part[0] += w * v0.x;
+    part[1] += w * v0.y;
+    part[2] += w * v0.z;
+    part[3] += w * v0.w;
+    part[4] += w * v1.x;
+    part[5] += w * v1.y;
+    part[6] += w * v1.z;
+    part[7] += w * v1.w;
   }
 }
 
@@ -203,8 +274,9 @@ __device__ __forceinline__ float ipow(float b, int e) {
 
 __global__ void __launch_bounds__(kThreads, FMKA_SCAN_MINB) route_ema_blend_kernel(const __grid_constant__ ScanParams p) {
   __shared__ uint32_t s_tile;
-  __shared__ float s_wagg[kWarps][kSlice];
-  __shared__ float s_in[kSlice];
+  __shared__ float4 s_wagg[kWarps][2][32];  // each warp's zero-state aggregate (put8 / get8 layout)
+  __shared__ float4 s_in[2][32];            // full look-back: the state entering the chunk
+  __shared__ float4 s_part[kWarps][2][32];  // short look-back: each warp's weighted predecessor sum
   __shared__ float s_lam[kChunkT][4];
 
   const int warp = warp_id();
@@ -288,36 +360,69 @@ __global__ void __launch_bounds__(kThreads, FMKA_SCAN_MINB) route_ema_blend_kern
 #pragma unroll
       for (int c = 0; c < 8; ++c) st[c] = p.beta * st[c] + p.one_minus_beta * xf[c];
     }
-#pragma unroll
-    for (int c = 0; c < 8; ++c) s_wagg[warp][lane * 8 + c] = st[c];
+    put8(s_wagg[warp], lane, st);
   }
   __syncthreads();
 
-  // ---- chunk aggregate + decoupled look-back (warp 0) ----
-  if (scan && warp == 0) {
-    float a[8];
+  // ---- chunk aggregate + look-back ----
+  const bool short_lb = p.lb_max > 0;  // grid-uniform
+  if (scan && short_lb) {
+    if (warp == 0) {
+      // publish this chunk's aggregate before waiting on anything
+      float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      float v = 0.f;
+      for (int w = 0; w < kWarps; ++w) {
+        float wa[8];
+        get8(s_wagg[w], lane, wa);
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) v = p.beta8 * v + s_wagg[w][lane * 8 + c];
-      a[c] = v;
+        for (int c = 0; c < 8; ++c) a[c] = p.beta8 * a[c] + wa[c];
+      }
+      const int64_t rec = (int64_t)seq * p.nchunks + chunk;
+      float4* dst = reinterpret_cast<float4*>(p.agg + rec * kSlice + lane * 8);
+      __stcg(dst, make_float4(a[0], a[1], a[2], a[3]));
+      __stcg(dst + 1, make_float4(a[4], a[5], a[6], a[7]));
+      __syncwarp();
+      if (lane == 0) st_release_u32(p.flags + rec, kFlagAgg);
+    }
+    if (warp < p.lb_max) {
+      float part[8];
+      short_lookback(p, seq, chunk, warp, part);
+      put8(s_part[warp], lane, part);
+    }
+  } else if (scan && warp == 0) {
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      float wa[8];
+      get8(s_wagg[w], lane, wa);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) a[c] = p.beta8 * a[c] + wa[c];
     }
     float sin_[8];
     chunk_lookback(p, seq, chunk, a, sin_);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) s_in[lane * 8 + c] = sin_[c];
+    put8(s_in, lane, sin_);
   }
   __syncthreads();
 
   // ---- state entering this warp's tokens ----
   float st[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   if (scan) {
+    if (short_lb) {
+      const int nparts = p.lb_max < kWarps ? p.lb_max : kWarps;
+      for (int w = 0; w < nparts; ++w) {
+        float v[8];
+        get8(s_part[w], lane, v);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      float v = s_in[lane * 8 + c];
-      for (int w = 0; w < warp; ++w) v = p.beta8 * v + s_wagg[w][lane * 8 + c];
-      st[c] = v;
+        for (int c = 0; c < 8; ++c) st[c] += v[c];
+      }
+    } else {
+      get8(s_in, lane, st);
+    }
+    for (int w = 0; w < warp; ++w) {
+      float v[8];
+      get8(s_wagg[w], lane, v);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) st[c] = p.beta8 * st[c] + v[c];
     }
     if (p.ema_init != nullptr && ch_ok) {
       // the scan runs from a zero state; a state s before token 0 adds
@@ -337,6 +442,13 @@ __global__ void __launch_bounds__(kThreads, FMKA_SCAN_MINB) route_ema_blend_kern
   }
 
   // ---- blend and store ----
+  float kvb[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // K/V bias of this lane's channels, loaded once
+  if (p.kv_k != nullptr && p.kv_bias != nullptr && ch_ok) {
+    const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.kv_bias + d0));
+    const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.kv_bias + d0 + 4));
+    kvb[0] = b0.x; kvb[1] = b0.y; kvb[2] = b0.z; kvb[3] = b0.w;
+    kvb[4] = b1.x; kvb[5] = b1.y; kvb[6] = b1.z; kvb[7] = b1.w;
+  }
 #pragma unroll
   for (int i = 0; i < kTokPerWarp; ++i) {
     const int t = tw + i;
@@ -377,12 +489,8 @@ __global__ void __launch_bounds__(kThreads, FMKA_SCAN_MINB) route_ema_blend_kern
       // 128-dim head pairs with d0 + c -/+ 64, which lives 8 lanes away.
       const int nk = p.D >> 1;  // K channels
       const bool is_k = d0 < nk;
-      if (p.kv_bias != nullptr && ch_ok) {
-        const float4 b0 = *reinterpret_cast<const float4*>(p.kv_bias + d0);
-        const float4 b1 = *reinterpret_cast<const float4*>(p.kv_bias + d0 + 4);
-        o[0] += b0.x; o[1] += b0.y; o[2] += b0.z; o[3] += b0.w;
-        o[4] += b1.x; o[5] += b1.y; o[6] += b1.z; o[7] += b1.w;
-      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) o[c] += kvb[c];
       const int dim = d0 & 127;  // position of this lane's 8 channels in their head
       if (p.rope_cos != nullptr) {
         float partner[8];
@@ -500,7 +608,21 @@ int launch_route_ema_blend(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, c
   p.beta = beta;
   p.one_minus_beta = 1.0f - beta;
   p.beta8 = (float)__builtin_powi((double)beta, 8);
-  p.beta64 = (float)__builtin_powi((double)beta, 64);
+  p.beta_chunk = (float)__builtin_powi((double)beta, kChunkT);
+  // the shortest look-back whose first left-out weight beta^(kChunkT k) is
+  // below 2^-40 (at most 32 chunks; otherwise the full look-back)
+  p.lb_max = 0;
+  {
+    const double b64 = std::fabs(__builtin_powi((double)beta, kChunkT));
+    double w = 1.0;
+    for (int k = 1; k <= 32; ++k) {
+      w *= b64;
+      if (w < 0x1p-40) {
+        p.lb_max = k;
+        break;
+      }
+    }
+  }
   p.B = B;
   p.T = T;
   p.D = D;
