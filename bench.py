@@ -711,6 +711,64 @@ def bench_model(args, device):
     return out
 
 
+def bench_model_sharded(args, dist, rank, world, device):
+    """The same full-model prefill over `world` GPUs of the box: every rank
+    holds the whole model; the sequence's residual rows, RMSNorms and MLP are
+    split by rows and the attention by kv heads (mka_b200.hf.sharded_llama):
+    one NCCL all-gather of the normed hidden states and one of the gate logits
+    per layer, and the attention output exchanged by the attention kernel's own
+    stores into peer memory. One 65536-token sequence per step (fixed total
+    work), device-timed, max over ranks."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from mka_b200.hf.patch import HFPatchConfig, apply_hf_attention_patch
+    from mka_b200.hf.sharded_llama import SequenceHeadShardedLlama
+
+    c = MODEL
+    cfg = LlamaConfig(vocab_size=c["vocab"], hidden_size=c["D"], intermediate_size=c["FFN"],
+                      num_hidden_layers=c["layers"], num_attention_heads=c["H"], num_key_value_heads=c["HKV"],
+                      max_position_embeddings=131072, rope_theta=c["theta"], attn_implementation="sdpa")
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(device):
+            torch.manual_seed(5)
+            model = LlamaForCausalLM(cfg).eval()
+            patched = apply_hf_attention_patch(model, HFPatchConfig(use_l3=True, verbose=False))
+    finally:
+        torch.set_default_dtype(prev)
+    g = torch.Generator(device=device).manual_seed(6)
+    ids = torch.randint(0, c["vocab"], (c["B"], c["T"]), generator=g, device=device)
+    l3 = (torch.randn(c["B"], c["T"], c["D"], generator=g, device=device) * 0.5).to(torch.bfloat16)
+    sh = SequenceHeadShardedLlama(model, rank, world)
+
+    def step():
+        sh(ids, l3_memory=l3)
+
+    step()  # warm-up: folds and shards each layer's weights, maps the peer regions
+    steps = max(1, min(args.steps, 3))
+    ms = _timed(dist, step, steps)
+    sh.close()
+    tokens = c["B"] * c["T"]
+    out = {
+        "metric": "Llama-3-8B prefill tokens/s, every self_attn patched with FastMKA, one sequence over the box",
+        "value": tokens / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "n_gpus": world,
+        "scaling": "strong", "patched_layers": patched,
+        "config": {"model": c["name"], "layers": c["layers"], "d_model": c["D"], "ffn": c["FFN"],
+                   "heads": f"{c['H']}/{c['HKV']}", "vocab": c["vocab"], "rope_theta": c["theta"],
+                   "batch": c["B"], "seq_len": c["T"], "logits": "last position",
+                   "levels": "L1 + L2 + L3 (L3: seeded N(0, 0.5) memory [1, 65536, 4096], the same for every layer)",
+                   "partition": f"rows {c['T'] // world} per rank (embeddings, RMSNorm, MLP, o_proj), "
+                                f"{c['HKV'] // world} kv head(s) per rank (q/k/v, scan, attention)",
+                   "collectives": "per layer: NCCL all-gather of the normed hidden states and of the gate logits; "
+                                  "attention rows exchanged by peer stores from the attention kernel"},
+        "data": "synthetic token ids U[0, vocab), random N(0, 0.02) bf16 weights",
+    }
+    del model, sh
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -769,8 +827,14 @@ def main():
             except Exception as e:  # a secondary line must not take the headline line down with it
                 model = {"error": f"{type(e).__name__}: {e}"[:400]}
                 torch.cuda.empty_cache()
+        elif MODEL["HKV"] % world == 0:
+            try:
+                model = bench_model_sharded(args, dist, rank, world, device)
+            except Exception as e:  # a secondary line must not take the headline line down with it
+                model = {"error": f"{type(e).__name__}: {e}"[:400]}
+                torch.cuda.empty_cache()
         else:
-            model = {"skipped": "the full-model line runs on one GPU (its FFN and embeddings are not sharded)"}
+            model = {"skipped": f"{MODEL['HKV']} kv heads do not split over {world} GPUs"}
     status = ops.device_status()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

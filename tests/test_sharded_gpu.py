@@ -6,6 +6,7 @@ barriers and the reused buffers are exercised), with two levels and with three
 (a per-position L3 memory, the long-context configuration's layer).
 Skipped with fewer GPUs than ranks."""
 import math
+import datetime
 import os
 
 import pytest
@@ -26,7 +27,7 @@ def _worker(rank, world, port, batch, transport, heads, levels, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         from tests.test_parity_gpu import _gqa_l3_layer
 
@@ -62,6 +63,11 @@ def _worker(rank, world, port, batch, transport, heads, levels, q):
             errs_cuda.append(((out.float() - r.float()).abs().max() / r.float().abs().max()).item())
         sh.close()
         q.put((rank, max(errs), max(errs_cuda), len(sh.plan.group), ops.device_status()))
+    except Exception:
+        import traceback
+
+        q.put((rank, "error", traceback.format_exc()))
+        raise
     finally:
         dist.destroy_process_group()
 
@@ -79,10 +85,18 @@ def test_head_sharded_layer_matches_oracle(world, batch, transport, heads, level
              for r in range(world)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=240) for _ in range(world)]
-    for p in procs:
-        p.join(timeout=60)
-        assert p.exitcode == 0
+    try:
+        res = [q.get(timeout=240) for _ in range(world)]
+        errors = [r for r in res if r[1] == "error"]
+        assert not errors, errors[0][2]
+        for p in procs:
+            p.join(timeout=60)
+            assert p.exitcode == 0
+    finally:
+        for p in procs:  # a rank that failed must not keep its GPU for the next test
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=30)
     for rank, err, err_cuda, gsize, status in res:
         assert status == 0
         assert gsize == max(world // batch, 1)
