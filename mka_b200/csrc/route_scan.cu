@@ -14,13 +14,13 @@
 // Parallel scan. The EMA is a linear recurrence, so the state after a chunk is
 // the chunk's zero-state scan ("aggregate") plus beta^len times the state that
 // entered it; a chunk only needs its incoming state S_in to finish. Each CTA
-// owns (batch row, 256-channel slice, 64-token chunk). Eight warps each scan
+// owns (batch row, 256-channel slice, 128-token chunk). Sixteen warps each scan
 // eight tokens with 128-bit loads (lane = 8 channels); warp aggregates are
 // combined in shared memory (two float4 planes per row, conflict-free). The
 // chunk's incoming state comes from the preceding chunks of the same (batch,
 // slice):
-//   * short memory (beta^(64 k) < 2^-40 within k <= 32 chunks, e.g. beta = 0.9:
-//     k = 5): the weighted sum of the k preceding chunk aggregates, read by k
+//   * short memory (beta^(128 k) < 2^-40 within k <= 32 chunks, e.g. beta = 0.9:
+//     k = 3): the weighted sum of the k preceding chunk aggregates, read by k
 //     warps in parallel. Older chunks weigh less than 2^-40 and are left out;
 //     no chunk waits on more than the aggregates of its k predecessors;
 //   * long memory: a decoupled look-back, each CTA publishing its aggregate,
@@ -28,11 +28,12 @@
 //     inclusive state.
 // Chunk order comes from an atomic ticket, so a CTA only ever waits on CTAs
 // that started before it. Waits are bounded; a timeout sets a status bit and the
-// scan continues with a zero contribution. Three CTAs share an SM so that one
-// CTA's waits are covered by the others' loads. Measured on the layer's K/V-mode
-// scan (batch 4 x 8192 tokens, 1024 channels): 0.121 ms with the [32][8]
+// scan continues with a zero contribution. Two CTAs share an SM so that one
+// CTA's waits are covered by the other's loads. Measured on the layer's K/V-mode
+// scan (batch 4 x 8192 tokens, 1024 channels): 0.121 ms with a [32][8]
 // shared-memory layout, whose eight-way bank conflicts kept the L1 pipe 74 %
-// busy, and 0.074 ms with the float4 planes.
+// busy; with the float4 planes 0.074 ms at 8 warps x 3 CTAs per SM and 0.071 ms
+// at 16 warps x 2 CTAs per SM.
 #include <mutex>
 
 #include "fmka_internal.h"
@@ -43,16 +44,16 @@ namespace fmka {
 namespace {
 
 #ifndef FMKA_SCAN_WARPS
-#define FMKA_SCAN_WARPS 8
+#define FMKA_SCAN_WARPS 16
 #endif
 constexpr int kWarps = FMKA_SCAN_WARPS;
 constexpr int kTokPerWarp = 8;
-constexpr int kChunkT = kWarps * kTokPerWarp;  // tokens per CTA (64)
+constexpr int kChunkT = kWarps * kTokPerWarp;  // tokens per CTA (128)
 constexpr int kSlice = 256;   // channels per CTA (32 lanes x 8)
 constexpr int kThreads = kWarps * 32;
 
 #ifndef FMKA_SCAN_MINB
-#define FMKA_SCAN_MINB 3
+#define FMKA_SCAN_MINB 2
 #endif
 constexpr uint32_t kFlagAgg = 1;
 constexpr uint32_t kFlagInc = 2;
@@ -71,7 +72,7 @@ struct ScanParams {
   int T3;
   float beta, one_minus_beta, beta8, beta_chunk;  // beta_chunk = beta^kChunkT
   // Short-memory look-back: when beta^(kChunkT * lb_max) < 2^-40 (beta <= ~0.98
-  // at 64-token chunks), the state entering a chunk is the sum of the lb_max
+  // at 128-token chunks), the state entering a chunk is the sum of the lb_max
   // preceding chunk aggregates weighted by beta^(kChunkT k); older chunks weigh less than 2^-40 of
   // the newest one, far below fp32 resolution, and are left out. Each chunk then
   // waits only for the aggregates of its lb_max predecessors (no inclusive
@@ -172,7 +173,7 @@ __device__ __forceinline__ void chunk_lookback(const ScanParams& p, int seq, int
     const uint32_t* seq_flags = p.flags + (int64_t)seq * p.nchunks;
     const int64_t seq_rec = (int64_t)seq * p.nchunks;
     int base = chunk - 1;  // nearest predecessor not yet accounted for
-    float mult = 1.f;      // beta^(64 * (chunk - 1 - base))
+    float mult = 1.f;      // beta^(kChunkT * (chunk - 1 - base))
     const uint64_t tstart = globaltimer_ns();
     while (true) {
       const int pc = base - lane;
@@ -223,7 +224,7 @@ __device__ __forceinline__ void chunk_lookback(const ScanParams& p, int seq, int
 
 // Short-memory look-back, run by every warp: warp w adds the aggregates of
 // predecessor chunks chunk-1-k, k = w, w + kWarps, ... < lb_max, each weighted
-// by beta^(64 k), into part (this lane's 8 channels). Every lane polls the flag
+// by beta^(kChunkT k), into part (this lane's 8 channels). Every lane polls the flag
 // (a broadcast load) so that each lane's own acquire orders its record reads.
 __device__ __forceinline__ void short_lookback(const ScanParams& p, int seq, int chunk, int warp, float (&part)[8]) {
   const int lane = lane_id();
@@ -613,10 +614,10 @@ int launch_route_ema_blend(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, c
   // below 2^-40 (at most 32 chunks; otherwise the full look-back)
   p.lb_max = 0;
   {
-    const double b64 = std::fabs(__builtin_powi((double)beta, kChunkT));
+    const double bc = std::fabs(__builtin_powi((double)beta, kChunkT));
     double w = 1.0;
     for (int k = 1; k <= 32; ++k) {
-      w *= b64;
+      w *= bc;
       if (w < 0x1p-40) {
         p.lb_max = k;
         break;
