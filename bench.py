@@ -549,7 +549,7 @@ def run_kernel_only(args):
     if args.only in ("attn_prefill", "route_ema_blend", "route_ema_blend_h", "qr_proj", "kv_gemm", "kv_proj",
                      "o_proj"):
         B = args.batch or c["B"]
-        T, D = c["T"], c["D"]
+        T, D = args.seq or c["T"], c["D"]
         if args.only == "attn_prefill":
             q = torch.randn(B, c["H"], T, 128, generator=g, device=dev, dtype=torch.bfloat16)
             k = torch.randn(B, c["HKV"], T, 128, generator=g, device=dev, dtype=torch.bfloat16)
@@ -610,8 +610,12 @@ def run_kernel_only(args):
         fn()
     e1.record()
     torch.cuda.synchronize()
-    print(json.dumps({"only": args.only, "launches": n, "ms_per_launch": e0.elapsed_time(e1) / max(args.steps, 1),
-                      "device_status": ops.device_status()}))
+    ms = e0.elapsed_time(e1) / max(args.steps, 1)
+    line = {"only": args.only, "launches": n, "ms_per_launch": ms, "device_status": ops.device_status()}
+    if args.only == "attn_prefill":
+        flops = 4.0 * B * c["H"] * 128 * T * (T + 1) / 2
+        line.update(batch=B, seq=T, tflops=round(flops / (ms * 1e-3) / 1e12, 1))
+    print(json.dumps(line))
 
 
 def _ref_config(threads):
@@ -788,6 +792,7 @@ def main():
                     help="run one kernel alone (attn_prefill, attn_decode, route_ema_blend, route_ema_blend_h, "
                          "qr_proj, kv_gemm, kv_proj, o_proj, o_proj_scatter, o_proj_blocked)")
     ap.add_argument("--batch", type=int, default=0, help="batch override for --only")
+    ap.add_argument("--seq", type=int, default=0, help="sequence-length override for --only (prefill kernels)")
     args = ap.parse_args()
     if args.only:
         run_kernel_only(args)

@@ -23,7 +23,7 @@
 //               tiles, running max m and sum z, writes P (bf16) back over S,
 //               rescales O in TMEM only when the max grew by more than 2^8
 //               (exact: the final 1/z uses the same stale max). One pair
-//               of exponentials in eight runs on the FMA pipe (exp2_poly2)
+//               of exponentials in sixteen runs on the FMA pipe (exp2_poly2)
 //               to relieve the special-function unit. At the end the
 //               warpgroup normalises O and writes O and LSE.
 // KV tiles past a Q tile's causal limit are neither loaded nor multiplied.
@@ -55,9 +55,13 @@ constexpr int kTileBytes = 128 * 128 * 2;   // 32 KB
 constexpr int kHalfBytes = kTileBytes / 2;  // one 64-column swizzle box
 constexpr int kSmemBytes = kTileBytes * (kQTiles + 2 * kKS) + 1024 + 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
-// One pair in every kPolyEvery pairs of exponentials runs on the FMA pipe.
+// One pair in every FMKA_POLY_EVERY pairs of exponentials runs on the FMA pipe.
+// Measured (batch 4 x 8192 and 1 x 32768, 28/4 heads, same box, two runs each):
+// one in 4: 1054 / 1169 TFLOP/s, one in 8: 1041-1051 / 1165-1176, one in 16:
+// 1081 / 1210, none: 1085 / 1201-1211. The softmax step is bound by its
+// latency, not by the MUFU's throughput, and the polynomial is the longer path.
 #ifndef FMKA_POLY_EVERY
-#define FMKA_POLY_EVERY 8
+#define FMKA_POLY_EVERY 16
 #endif
 // Pack P to bf16 with integer rounding (ALU pipe) instead of cvt (XU pipe).
 #ifndef FMKA_PACK_ALU

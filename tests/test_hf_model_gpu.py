@@ -139,7 +139,8 @@ def test_mlp_fusion_walks_layers_and_keeps_parameter_names():
 
 @pytest.mark.gpu
 def test_fused_mlp_matches_transformers_mlp():
-    """A patched LlamaForCausalLM with the fused MLP against the same model with
+    """The fused MLP of one layer against an fp32 SwiGLU MLP on the CPU, and a
+    patched LlamaForCausalLM with the fused MLP against the same model with
     transformers' MLP (both bf16 on the GPU, self_attn patched in both)."""
     from mka_b200.hf.mlp import FusedSwiGLUMLP, apply_mlp_fusion
 
@@ -153,6 +154,12 @@ def test_fused_mlp_matches_transformers_mlp():
     with torch.no_grad():
         mlp = model.model.layers[0].mlp
         fm = FusedSwiGLUMLP(mlp)
+        # an fp32 SwiGLU MLP with the same (bf16) weights on the CPU: down(silu(gate x) * up x)
+        f32 = lambda lin: lin.weight.detach().float().cpu()  # noqa: E731
+        xf = x.float().cpu()
+        ref = torch.nn.functional.silu(xf @ f32(mlp.gate_proj).T) * (xf @ f32(mlp.up_proj).T)
+        ref = ref @ f32(mlp.down_proj).T
+        assert _rel(fm(x), ref) < 2e-2
         assert _rel(fm(x), mlp(x)) < 2e-2
         ids = torch.randint(0, 128, (2, 96), generator=g).cuda()
         a = model(ids).logits
