@@ -223,7 +223,9 @@ def test_ema_carried_state(ops, T1, T2, D, beta):
 
 @pytest.mark.parametrize("B,Hq,Hkv,Tq,Tk,causal", [(1, 1, 1, 128, 128, True), (2, 4, 2, 200, 200, True),
                                                    (1, 7, 1, 300, 300, True), (2, 2, 2, 64, 333, True),
-                                                   (1, 2, 1, 130, 257, False), (1, 4, 4, 1024, 1024, True)])
+                                                   (1, 2, 1, 130, 257, False), (1, 4, 4, 1024, 1024, True),
+                                                   (1, 2, 1, 700, 1500, True), (2, 3, 3, 520, 520, False),
+                                                   (1, 7, 1, 1536, 1536, True)])
 def test_attn_prefill(ops, B, Hq, Hkv, Tq, Tk, causal):
     g = torch.Generator(device="cuda").manual_seed(Tq * 7 + Tk)
     q = torch.randn(B, Hq, Tq, 128, device="cuda", generator=g).bfloat16()
