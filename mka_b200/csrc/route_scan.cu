@@ -14,13 +14,13 @@
 // Parallel scan. The EMA is a linear recurrence, so the state after a chunk is
 // the chunk's zero-state scan ("aggregate") plus beta^len times the state that
 // entered it; a chunk only needs its incoming state S_in to finish. Each CTA
-// owns (batch row, 256-channel slice, 128-token chunk). Sixteen warps each scan
+// owns (batch row, 256-channel slice, 64-token chunk). Eight warps each scan
 // eight tokens with 128-bit loads (lane = 8 channels); warp aggregates are
 // combined in shared memory (two float4 planes per row, conflict-free). The
 // chunk's incoming state comes from the preceding chunks of the same (batch,
 // slice):
-//   * short memory (beta^(128 k) < 2^-40 within k <= 32 chunks, e.g. beta = 0.9:
-//     k = 3): the weighted sum of the k preceding chunk aggregates, read by k
+//   * short memory (beta^(64 k) < 2^-40 within k <= 32 chunks, e.g. beta = 0.9:
+//     k = 5): the weighted sum of the k preceding chunk aggregates, read by k
 //     warps in parallel. Older chunks weigh less than 2^-40 and are left out;
 //     no chunk waits on more than the aggregates of its k predecessors;
 //   * long memory: a decoupled look-back, each CTA publishing its aggregate,
@@ -28,12 +28,19 @@
 //     inclusive state.
 // Chunk order comes from an atomic ticket, so a CTA only ever waits on CTAs
 // that started before it. Waits are bounded; a timeout sets a status bit and the
-// scan continues with a zero contribution. Two CTAs share an SM so that one
-// CTA's waits are covered by the other's loads. Measured on the layer's K/V-mode
-// scan (batch 4 x 8192 tokens, 1024 channels): 0.121 ms with a [32][8]
-// shared-memory layout, whose eight-way bank conflicts kept the L1 pipe 74 %
-// busy; with the float4 planes 0.074 ms at 8 warps x 3 CTAs per SM and 0.071 ms
-// at 16 warps x 2 CTAs per SM.
+// scan continues with a zero contribution. Three CTAs share an SM so that one
+// CTA's waits are covered by the others' loads.
+//
+// Two kernels. route_ema_blend_kernel covers every mode (H or K/V output, a
+// given L2, a carried EMA state, long memory). kv_scan_kernel is the layer's
+// case (K/V output, short memory, no carried state) with the mode fixed at
+// compile time and the state scaled by 1 / (1 - beta), one FMA per step.
+// Measured on the layer's K/V-mode scan (batch 4 x 8192 tokens, 1024
+// channels): 0.121 ms with a [32][8] shared-memory layout, whose eight-way bank
+// conflicts kept the L1 pipe 74 % busy; 0.071-0.074 ms for the general kernel
+// with the float4 planes; 0.058 ms for kv_scan_kernel (0.060 at 16 warps x
+// 128-token chunks, 2 CTAs per SM).
+#include <cstdlib>
 #include <mutex>
 
 #include "fmka_internal.h"
@@ -44,16 +51,16 @@ namespace fmka {
 namespace {
 
 #ifndef FMKA_SCAN_WARPS
-#define FMKA_SCAN_WARPS 16
+#define FMKA_SCAN_WARPS 8
 #endif
 constexpr int kWarps = FMKA_SCAN_WARPS;
 constexpr int kTokPerWarp = 8;
-constexpr int kChunkT = kWarps * kTokPerWarp;  // tokens per CTA (128)
+constexpr int kChunkT = kWarps * kTokPerWarp;  // tokens per CTA (64)
 constexpr int kSlice = 256;   // channels per CTA (32 lanes x 8)
 constexpr int kThreads = kWarps * 32;
 
 #ifndef FMKA_SCAN_MINB
-#define FMKA_SCAN_MINB 2
+#define FMKA_SCAN_MINB 3
 #endif
 constexpr uint32_t kFlagAgg = 1;
 constexpr uint32_t kFlagInc = 2;
@@ -532,7 +539,212 @@ __global__ void __launch_bounds__(kThreads, FMKA_SCAN_MINB) route_ema_blend_kern
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// The layer's stage 1 as a specialised kernel: K/V output, short look-back,
+// no carried EMA state, whole 256-channel slices. The same chunking and
+// look-back as route_ema_blend_kernel, with the mode decided at compile time
+// (RoPE, bias, third level) and the state kept scaled: u_t = beta u_{t-1} + y_t,
+// so that EMA_t = (1 - beta) u_t and each step is one FMA; the factor (1 - beta)
+// moves into the gate (lam1 (1 - beta)) and the chunk aggregates and the
+// look-back work in u units throughout. Base pointers are formed once per
+// thread and advanced by their strides; only the stores of the last chunk's
+// rows past T are predicated (those rows read row T - 1 and come after every
+// valid token, so they change only an aggregate that no chunk reads).
+template <bool kRope, bool kBias, bool kL3>
+__global__ void __launch_bounds__(kThreads, FMKA_SCAN_MINB) kv_scan_kernel(const __grid_constant__ ScanParams p) {
+  __shared__ uint32_t s_tile;
+  __shared__ float4 s_wagg[kWarps][2][32];
+  __shared__ float4 s_part[kWarps][2][32];
+  __shared__ float4 s_gate[kChunkT];  // lam0, lam1 (1 - beta), lam2 per token
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  if (threadIdx.x == 0) s_tile = atomicAdd(p.ticket, 1u);
+  __syncthreads();
+  const int tile = static_cast<int>(s_tile);
+  const int nseq = p.B * p.nds;
+  const int chunk = tile / nseq;
+  const int seq = tile % nseq;
+  const int b = seq / p.nds;
+  const int ds = seq % p.nds;
+  const int T = p.T;
+  const int t0 = chunk * kChunkT;
+  const int tw = t0 + warp * kTokPerWarp;
+  const int d0 = ds * kSlice + lane * 8;
+  const float beta = p.beta;
+
+  // ---- this warp's 8 rows x 8 channels per lane (read again, from L1, by
+  // the blend, so that they are not held in registers across the look-back) ----
+  const __nv_bfloat16* xw = p.x + (int64_t)b * p.x_sb + d0 + (int64_t)tw * p.x_st;
+  const int last = T - 1 - tw;  // rows i > last repeat row T - 1
+  uint4 xr[kTokPerWarp];
+#pragma unroll
+  for (int i = 0; i < kTokPerWarp; ++i)
+    xr[i] = __ldg(reinterpret_cast<const uint4*>(xw + (int64_t)(i < last ? i : last) * p.x_st));
+  // ---- gate of the chunk's tokens ----
+  if (threadIdx.x < kChunkT) {
+    const int t = t0 + threadIdx.x;
+    float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (t < T) {
+      const int64_t row = (int64_t)b * T + t;
+      const float* lg = p.logits + row * p.L;
+      float a0 = lg[0] + (p.b2 ? p.b2[0] : 0.f);
+      float a1 = lg[1] + (p.b2 ? p.b2[1] : 0.f);
+      float a2 = kL3 ? lg[2] + (p.b2 ? p.b2[2] : 0.f) : -INFINITY;
+      const float mx = fmaxf(fmaxf(a0, a1), a2);
+      a0 = __expf(a0 - mx);
+      a1 = __expf(a1 - mx);
+      a2 = kL3 ? __expf(a2 - mx) : 0.f;
+      const float inv = 1.f / (a0 + a1 + a2);
+      a0 *= inv;
+      a1 *= inv;
+      a2 *= inv;
+      if (p.lam != nullptr && ds == 0) {
+        p.lam[row * p.L] = a0;
+        p.lam[row * p.L + 1] = a1;
+        if (kL3) p.lam[row * p.L + 2] = a2;
+      }
+      g = make_float4(a0, a1 * p.one_minus_beta, a2, 0.f);
+    }
+    s_gate[threadIdx.x] = g;
+  }
+
+  // ---- zero-state scan of this warp's 8 tokens (u units) ----
+  {
+    float u[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < kTokPerWarp; ++i) {
+      float xf[8];
+      unpack8(xr[i], xf);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) u[c] = fmaf(beta, u[c], xf[c]);
+    }
+    put8(s_wagg[warp], lane, u);
+  }
+  __syncthreads();
+
+  // ---- chunk aggregate, then the k preceding chunks' aggregates ----
+  if (warp == 0) {
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      float wa[8];
+      get8(s_wagg[w], lane, wa);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) a[c] = fmaf(p.beta8, a[c], wa[c]);
+    }
+    const int64_t rec = (int64_t)seq * p.nchunks + chunk;
+    float4* dst = reinterpret_cast<float4*>(p.agg + rec * kSlice + lane * 8);
+    __stcg(dst, make_float4(a[0], a[1], a[2], a[3]));
+    __stcg(dst + 1, make_float4(a[4], a[5], a[6], a[7]));
+    __syncwarp();
+    if (lane == 0) st_release_u32(p.flags + rec, kFlagAgg);
+  }
+  const int nparts = p.lb_max < kWarps ? p.lb_max : kWarps;
+  if (warp < nparts) {
+    float part[8];
+    short_lookback(p, seq, chunk, warp, part);
+    put8(s_part[warp], lane, part);
+  }
+  __syncthreads();
+
+  // ---- state entering this warp's tokens ----
+  float u[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int w = 0; w < nparts; ++w) {
+    float v[8];
+    get8(s_part[w], lane, v);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) u[c] += v[c];
+  }
+  for (int w = 0; w < warp; ++w) {
+    float v[8];
+    get8(s_wagg[w], lane, v);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) u[c] = fmaf(p.beta8, u[c], v[c]);
+  }
+
+  // ---- blend, bias, RoPE, head-split store ----
+  const int nk = p.D >> 1;
+  const bool is_k = d0 < nk;
+  const int dim = d0 & 127;
+  const int head = (is_k ? d0 : d0 - nk) >> 7;
+  __nv_bfloat16* dst = (is_k ? p.kv_k : p.kv_v) + (int64_t)b * p.kv_sb + (int64_t)head * p.kv_sh +
+                       (int64_t)(tw + p.t_offset) * p.kv_st + dim;
+  float kvb[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (kBias) {
+    const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.kv_bias + d0));
+    const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.kv_bias + d0 + 4));
+    kvb[0] = b0.x; kvb[1] = b0.y; kvb[2] = b0.z; kvb[3] = b0.w;
+    kvb[4] = b1.x; kvb[5] = b1.y; kvb[6] = b1.z; kvb[7] = b1.w;
+  }
+  const float* cosp = nullptr;
+  const float* sinp = nullptr;
+  uint32_t sign_flip = 0u;  // rotate_half: the first 64 dims take -x2 (sign bit flipped)
+  if (kRope) {
+    cosp = p.rope_cos + (int64_t)b * p.rope_sb + (int64_t)tw * p.rope_st + dim;
+    sinp = p.rope_sin + (int64_t)b * p.rope_sb + (int64_t)tw * p.rope_st + dim;
+    sign_flip = dim < 64 ? 0x80000000u : 0u;
+  }
+  const __nv_bfloat16* y3p = nullptr;
+  if (kL3) y3p = p.l3 + (int64_t)b * p.l3_sb + d0;
+#pragma unroll
+  for (int i = 0; i < kTokPerWarp; ++i) {
+    const int t = tw + i;
+    const float4 g = s_gate[warp * kTokPerWarp + i];
+    float xf[8];
+    unpack8(__ldg(reinterpret_cast<const uint4*>(xw + (int64_t)(i < last ? i : last) * p.x_st)), xf);
+    float o[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      u[c] = fmaf(beta, u[c], xf[c]);
+      o[c] = fmaf(g.x, xf[c], fmaf(g.y, u[c], kvb[c]));
+    }
+    if (kL3) {
+      const int t3 = t < p.T3 ? t : p.T3 - 1;
+      float y3f[8];
+      unpack8(__ldcs(reinterpret_cast<const uint4*>(y3p + (int64_t)t3 * p.l3_st)), y3f);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) o[c] = fmaf(g.z, y3f[c], o[c]);
+    }
+    if (kRope) {
+      float partner[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) partner[c] = __shfl_xor_sync(0xffffffffu, o[c], 8);
+      if (is_k && t < T) {
+        const float4 c0 = __ldg(reinterpret_cast<const float4*>(cosp + (int64_t)i * p.rope_st));
+        const float4 c1 = __ldg(reinterpret_cast<const float4*>(cosp + (int64_t)i * p.rope_st + 4));
+        const float4 s0 = __ldg(reinterpret_cast<const float4*>(sinp + (int64_t)i * p.rope_st));
+        const float4 s1 = __ldg(reinterpret_cast<const float4*>(sinp + (int64_t)i * p.rope_st + 4));
+        const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+        const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          o[c] = fmaf(__uint_as_float(__float_as_uint(partner[c]) ^ sign_flip), sn[c], o[c] * cs[c]);
+      }
+    }
+    if (t < T) {
+      uint4 w;
+      w.x = pack_bf16x2(o[0], o[1]);
+      w.y = pack_bf16x2(o[2], o[3]);
+      w.z = pack_bf16x2(o[4], o[5]);
+      w.w = pack_bf16x2(o[6], o[7]);
+      *reinterpret_cast<uint4*>(dst + (int64_t)i * p.kv_st) = w;
+    }
+  }
+}
+
 }  // namespace
+
+// FMKA_SCAN_GENERAL=1 sends the layer's K/V scan to the general kernel too
+// (for comparisons; both compute the same function).
+static bool scan_general_forced() {
+  static const bool on = [] {
+    const char* e = std::getenv("FMKA_SCAN_GENERAL");
+    return e != nullptr && e[0] == '1';
+  }();
+  return on;
+}
 
 size_t route_ema_blend_workspace_bytes(int B, int T, int D) {
   const int64_t nds = (D + kSlice - 1) / kSlice;
@@ -669,6 +881,17 @@ int launch_route_ema_blend(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, c
   }
   const int64_t grid = nrec;
   if (grid > 0x7FFFFFFF) return set_error(kErrUnsupported, "route_ema_blend: problem too large");
+  if (kv != nullptr && l2 == nullptr && p.lb_max > 0 && ema_init == nullptr && ema_final == nullptr &&
+      logits != nullptr && D % kSlice == 0 && !scan_general_forced()) {
+    // the layer's case: the specialised kernel
+    const bool rope = p.rope_cos != nullptr, bias = p.kv_bias != nullptr, l3v = p.l3 != nullptr;
+    auto kern = rope ? (bias ? (l3v ? kv_scan_kernel<true, true, true> : kv_scan_kernel<true, true, false>)
+                             : (l3v ? kv_scan_kernel<true, false, true> : kv_scan_kernel<true, false, false>))
+                     : (bias ? (l3v ? kv_scan_kernel<false, true, true> : kv_scan_kernel<false, true, false>)
+                             : (l3v ? kv_scan_kernel<false, false, true> : kv_scan_kernel<false, false, false>));
+    kern<<<(unsigned)grid, kThreads, 0, stream>>>(p);
+    return check_cuda(cudaGetLastError(), "kv_scan launch");
+  }
   route_ema_blend_kernel<<<(unsigned)grid, kThreads, 0, stream>>>(p);
   return check_cuda(cudaGetLastError(), "route_ema_blend launch");
 }

@@ -147,12 +147,16 @@ def test_causal_prefix_ema_op(ops):
     assert _rel(out, _ref_ema(x.float(), 0.9)) < 1e-2
 
 
-@pytest.mark.parametrize("B,T,Hkv,rope,off,T3", [(2, 300, 4, True, 0, 0), (3, 65, 1, True, 7, 0),
-                                             (1, 1, 2, False, 5, 0), (2, 130, 8, True, 0, 0), (4, 64, 4, False, 0, 0),
-                                             (2, 300, 4, True, 0, 1), (3, 65, 1, True, 7, 40)])
-def test_route_ema_blend_kv(ops, B, T, Hkv, rope, off, T3):
+@pytest.mark.parametrize("B,T,Hkv,rope,off,T3,beta,with_bias", [
+    (2, 300, 4, True, 0, 0, 0.9, True), (3, 65, 1, True, 7, 0, 0.9, True), (1, 1, 2, False, 5, 0, 0.9, True),
+    (2, 130, 8, True, 0, 0, 0.9, True), (4, 64, 4, False, 0, 0, 0.9, True), (2, 300, 4, True, 0, 1, 0.9, True),
+    (3, 65, 1, True, 7, 40, 0.9, True), (2, 1000, 2, True, 3, 0, 0.9, False), (1, 700, 2, False, 0, 300, 0.5, False),
+    (2, 600, 1, True, 0, 0, 0.99, True)])
+def test_route_ema_blend_kv(ops, B, T, Hkv, rope, off, T3, beta, with_bias):
     """Stage 1 on y = x [Wk ; Wv]^T: K/V = lam0 y + lam1 EMA(y) (+ lam2 y3) + bias,
-    RoPE on K, head-split at token slot t + off; y3 row t is min(t, T3 - 1)."""
+    RoPE on K, head-split at token slot t + off; y3 row t is min(t, T3 - 1).
+    beta 0.99 takes the full look-back (the general kernel), the others the
+    short one (the specialised K/V kernel)."""
     N = 2 * Hkv * 128
     L = 3 if T3 else 2
     g = torch.Generator(device="cuda").manual_seed(B * 1000 + T)
@@ -160,18 +164,20 @@ def test_route_ema_blend_kv(ops, B, T, Hkv, rope, off, T3):
     logits = torch.randn(B * T, L, device="cuda", generator=g)
     b2 = torch.randn(L, device="cuda", generator=g)
     y3 = torch.randn(B, T3, N, device="cuda", generator=g).bfloat16() if T3 else None
-    bias = torch.randn(N, device="cuda", generator=g) * 0.1
+    bias = torch.randn(N, device="cuda", generator=g) * 0.1 if with_bias else None
     cs = None
     if rope:
         ang = torch.rand(B, T, 128, device="cuda", generator=g) * 6
         cs = (ang.cos(), ang.sin())
     kc = torch.zeros(B, Hkv, T + off + 3, 128, device="cuda", dtype=torch.bfloat16)
     vc = torch.zeros_like(kc)
-    _, _, lam = ops.route_ema_blend_kv(y, 0.9, logits, b2, B, T, Hkv, bias=bias, rope=cs, k_out=kc, v_out=vc,
+    _, _, lam = ops.route_ema_blend_kv(y, beta, logits, b2, B, T, Hkv, bias=bias, rope=cs, k_out=kc, v_out=vc,
                                        t_offset=off, y3=y3)
     lam_ref = torch.softmax(logits + b2, -1).view(B, T, L)
     yf = y.float().view(B, T, N)
-    blend = lam_ref[..., 0:1] * yf + lam_ref[..., 1:2] * _ref_ema(yf, 0.9) + bias
+    blend = lam_ref[..., 0:1] * yf + lam_ref[..., 1:2] * _ref_ema(yf, beta)
+    if bias is not None:
+        blend = blend + bias
     if T3:
         idx = torch.clamp(torch.arange(T, device="cuda"), max=T3 - 1)
         blend = blend + lam_ref[..., 2:3] * y3.float()[:, idx]

@@ -81,9 +81,9 @@ def test_workspace_sizes():
 
     lib = _lib.load()
     # route/EMA: ticket + flags (256-aligned) + two fp32 [records, 256] arrays, one
-    # record per (batch row, 256-channel slice, 128-token chunk)
+    # record per (batch row, 256-channel slice, 64-token chunk)
     B, T, D = 4, 8192, 3584
-    nrec = B * ((D + 255) // 256) * ((T + 127) // 128)
+    nrec = B * ((D + 255) // 256) * ((T + 63) // 64)
     flag_bytes = ((nrec * 4 + 256 + 255) // 256) * 256
     assert lib.fmka_route_ema_blend_workspace_size(B, T, D) == flag_bytes + 2 * nrec * 256 * 4
     assert lib.fmka_route_ema_blend_workspace_size(0, 1, 1) == 0
