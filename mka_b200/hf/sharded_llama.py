@@ -38,7 +38,7 @@ import torch.nn as nn
 from .. import ops
 from ..layers.prepared import PreparedWeights
 from ..peer import PeerRegion, bf16_view
-from ..sharded import shard_weights
+from ..sharded import raise_on_peer_timeout, shard_weights
 from .attention import HFFastMKAAttention
 from .patch import _iter_layers
 
@@ -53,9 +53,15 @@ class SequenceHeadShardedLlama:
     Collective: construct, call and `close()` on every rank in the same order,
     with the default process group initialised (NCCL). Needs the kv heads and
     the sequence length to split evenly over the ranks.
+
+    With `check_peer_status` (the default) each forward ends by reading the
+    device status word once and raises PeerExchangeError if one of its peer
+    barriers ran out of time (a rank never arrived, so some rows are missing);
+    pass False to keep the stream asynchronous and poll `ops.device_status()`.
     """
 
-    def __init__(self, model: nn.Module, rank: int, world: int, group=None):
+    def __init__(self, model: nn.Module, rank: int, world: int, group=None, check_peer_status: bool = True):
+        self.check_peer_status = check_peer_status
         self.model = model
         self.rank, self.world, self.group = rank, world, group
         self.layers = list(_iter_layers(model))
@@ -166,6 +172,8 @@ class SequenceHeadShardedLlama:
             o = ops.gemm_kblocked(gathered, Wl.w_o, Wl.b_o).view(1, rows, D)
             h = h + o.to(h.dtype)
             h = h + layer.mlp(layer.post_attention_layernorm(h))
+        if self.check_peer_status:
+            raise_on_peer_timeout()
         logits = m.lm_head(inner.norm(h[:, -1:])) if self.rank == W_ - 1 else None
         if return_hidden:
             return logits, inner.norm(h)
