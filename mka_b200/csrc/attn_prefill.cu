@@ -63,6 +63,11 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 #ifndef FMKA_POLY_EVERY
 #define FMKA_POLY_EVERY 16
 #endif
+// L2 policies on the TMA loads (Q evict-first, K/V evict-last) and streaming O
+// stores, so that K/V stay in L2 for the other query heads and blocks.
+#ifndef FMKA_ATTN_L2_HINTS
+#define FMKA_ATTN_L2_HINTS 1
+#endif
 // Pack P to bf16 with integer rounding (ALU pipe) instead of cvt (XU pipe).
 #ifndef FMKA_PACK_ALU
 #define FMKA_PACK_ALU 0
@@ -203,11 +208,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
       const int nt[2] = {n0, n1};
+#if FMKA_ATTN_L2_HINTS
+      // Q is read by one CTA only; K/V are read again by the other query heads
+      // of the group and the other query blocks: keep those in L2
+      const uint64_t pol_q = make_l2_policy_evict_first();
+      const uint64_t pol_kv = make_l2_policy_evict_last();
+#endif
       for (int i = 0; i < kQTiles; ++i) {
         if (nt[i] == 0) continue;
         mbar_arrive_expect_tx(&q_full[i], kTileBytes);
+#if FMKA_ATTN_L2_HINTS
+        tma_load_4d_hint(sQ + i * kTileBytes, &tmQ, &q_full[i], 0, q0 + i * kBM, hq, b, pol_q);
+        tma_load_4d_hint(sQ + i * kTileBytes + kHalfBytes, &tmQ, &q_full[i], 64, q0 + i * kBM, hq, b, pol_q);
+#else
         tma_load_4d(sQ + i * kTileBytes, &tmQ, &q_full[i], 0, q0 + i * kBM, hq, b);
         tma_load_4d(sQ + i * kTileBytes + kHalfBytes, &tmQ, &q_full[i], 64, q0 + i * kBM, hq, b);
+#endif
       }
       int last_k = -1, last_v = -1;
       for (int j = 0; j < n_load && !*abort_flag; ++j) {
@@ -218,16 +234,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(&k_full[ks], kTileBytes);
+#if FMKA_ATTN_L2_HINTS
+        tma_load_4d_hint(sK + ks * kTileBytes, &tmK, &k_full[ks], 0, j * kBN, hkv, b, pol_kv);
+        tma_load_4d_hint(sK + ks * kTileBytes + kHalfBytes, &tmK, &k_full[ks], 64, j * kBN, hkv, b, pol_kv);
+#else
         tma_load_4d(sK + ks * kTileBytes, &tmK, &k_full[ks], 0, j * kBN, hkv, b);
         tma_load_4d(sK + ks * kTileBytes + kHalfBytes, &tmK, &k_full[ks], 64, j * kBN, hkv, b);
+#endif
         last_k = j;
         if (!mbar_wait(&v_empty[ks], ph ^ 1u, p.status)) {
           *abort_flag = 1;
           break;
         }
         mbar_arrive_expect_tx(&v_full[ks], kTileBytes);
+#if FMKA_ATTN_L2_HINTS
+        tma_load_4d_hint(sV + ks * kTileBytes, &tmV, &v_full[ks], 0, j * kBN, hkv, b, pol_kv);
+        tma_load_4d_hint(sV + ks * kTileBytes + kHalfBytes, &tmV, &v_full[ks], 64, j * kBN, hkv, b, pol_kv);
+#else
         tma_load_4d(sV + ks * kTileBytes, &tmV, &v_full[ks], 0, j * kBN, hkv, b);
         tma_load_4d(sV + ks * kTileBytes + kHalfBytes, &tmV, &v_full[ks], 64, j * kBN, hkv, b);
+#endif
         last_v = j;
       }
       // Drain: every issued TMA load has landed before teardown (on the normal
@@ -450,7 +476,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               w.y = pack_bf16x2(__uint_as_float(o[v * 8 + 2]) * inv, __uint_as_float(o[v * 8 + 3]) * inv);
               w.z = pack_bf16x2(__uint_as_float(o[v * 8 + 4]) * inv, __uint_as_float(o[v * 8 + 5]) * inv);
               w.w = pack_bf16x2(__uint_as_float(o[v * 8 + 6]) * inv, __uint_as_float(o[v * 8 + 7]) * inv);
+#if FMKA_ATTN_L2_HINTS
+              if (p.o_rows_per_dst > 0) d4[v] = w;  // peer stores: plain
+              else __stcs(d4 + v, w);               // written once, read by the next kernel
+#else
               d4[v] = w;
+#endif
             }
           }
         }
