@@ -654,6 +654,7 @@ def bench_model(args, device):
     from transformers import LlamaConfig, LlamaForCausalLM
 
     from mka_b200.hf.mlp import apply_mlp_fusion
+    from mka_b200.hf.norm import apply_norm_fusion
     from mka_b200.hf.patch import HFPatchConfig, apply_hf_attention_patch
 
     c = MODEL
@@ -668,6 +669,7 @@ def bench_model(args, device):
             model = LlamaForCausalLM(cfg).eval()
             patched = apply_hf_attention_patch(model, HFPatchConfig(use_l3=True, verbose=False))
             fused_mlp = apply_mlp_fusion(model) if args.model_mlp == "fused" else 0
+            fused_norms = apply_norm_fusion(model) if args.model_norm == "fused" else 0
     finally:
         torch.set_default_dtype(prev)
     g = torch.Generator(device=device).manual_seed(6)
@@ -698,7 +700,7 @@ def bench_model(args, device):
     out = {
         "metric": "Llama-3-8B prefill tokens/s, every self_attn patched with FastMKA (transformers model)",
         "value": tokens / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
-        "patched_layers": patched, "fused_mlp_layers": fused_mlp,
+        "patched_layers": patched, "fused_mlp_layers": fused_mlp, "fused_norms": fused_norms,
         "fastmka_self_attn_ms_per_layer": attn_ms,
         "fastmka_self_attn_share": round(attn_ms * c["layers"] / ms, 4),
         "attention_tflops_per_layer": attn_flops / 1e12,
@@ -707,7 +709,9 @@ def bench_model(args, device):
                    "batch": c["B"], "seq_len": c["T"], "logits": "last position",
                    "levels": "L1 + L2 + L3 (L3: seeded N(0, 0.5) memory [1, 65536, 4096], the same for every layer)",
                    "mlp": ("gate/up GEMM with the SiLU-product epilogue, then down_proj (FusedSwiGLUMLP)"
-                           if fused_mlp else "transformers LlamaMLP (cuBLAS GEMMs + elementwise)")},
+                           if fused_mlp else "transformers LlamaMLP (cuBLAS GEMMs + elementwise)"),
+                   "norms": ("one-pass RMSNorm kernel (FusedRMSNorm)" if fused_norms
+                             else "transformers LlamaRMSNorm (elementwise kernels)")},
         "data": "synthetic token ids U[0, vocab), random N(0, 0.02) bf16 weights",
     }
     del model
@@ -725,6 +729,7 @@ def bench_model_sharded(args, dist, rank, world, device):
     work), device-timed, max over ranks."""
     from transformers import LlamaConfig, LlamaForCausalLM
 
+    from mka_b200.hf.norm import apply_norm_fusion
     from mka_b200.hf.patch import HFPatchConfig, apply_hf_attention_patch
     from mka_b200.hf.sharded_llama import SequenceHeadShardedLlama
 
@@ -739,6 +744,7 @@ def bench_model_sharded(args, dist, rank, world, device):
             torch.manual_seed(5)
             model = LlamaForCausalLM(cfg).eval()
             patched = apply_hf_attention_patch(model, HFPatchConfig(use_l3=True, verbose=False))
+            fused_norms = apply_norm_fusion(model) if args.model_norm == "fused" else 0
     finally:
         torch.set_default_dtype(prev)
     g = torch.Generator(device=device).manual_seed(6)
@@ -758,7 +764,7 @@ def bench_model_sharded(args, dist, rank, world, device):
     out = {
         "metric": "Llama-3-8B prefill tokens/s, every self_attn patched with FastMKA, one sequence over the box",
         "value": tokens / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "n_gpus": world,
-        "scaling": "strong", "patched_layers": patched,
+        "scaling": "strong", "patched_layers": patched, "fused_norms": fused_norms,
         "config": {"model": c["name"], "layers": c["layers"], "d_model": c["D"], "ffn": c["FFN"],
                    "heads": f"{c['H']}/{c['HKV']}", "vocab": c["vocab"], "rope_theta": c["theta"],
                    "batch": c["B"], "seq_len": c["T"], "logits": "last position",
@@ -787,6 +793,8 @@ def main():
                     help="how a head-sharded sequence group exchanges rows (long context, N > 2)")
     ap.add_argument("--model-mlp", choices=["fused", "transformers"], default="transformers",
                     help="the full-model line's MLP: transformers' own (default) or the fused SwiGLU GEMM")
+    ap.add_argument("--model-norm", choices=["fused", "transformers"], default="fused",
+                    help="the full-model line's RMSNorms: the one-pass kernel (default) or transformers' own")
     ap.add_argument("--no-model", action="store_true",
                     help="skip the full Llama-3-8B model measurement (one GPU only)")
     ap.add_argument("--only", default=None,

@@ -42,6 +42,9 @@
  *   fmka_gemm_bf16_swiglu   outside the attention path: the gate/up projections and
  *                           SiLU product of the Llama MLP around the patched
  *                           self_attn (transformers LlamaMLP), one GEMM
+ *   fmka_rmsnorm_bf16       outside the attention path: the RMSNorm of the decoder
+ *                           layers around the patched self_attn (transformers
+ *                           LlamaRMSNorm / Qwen2RMSNorm), one pass
  *   fmka_attn_fwd_prefill_scatter, fmka_gemm_bf16_kblocked_scatter, fmka_peer_*
  *                           the head-sharded layer over several GPUs of a box:
  *                           attention rows and o_proj rows stored straight into
@@ -247,6 +250,15 @@ FMKA_API int fmka_attn_decode_splitkv(const void* q, int64_t q_sb, int64_t q_sh,
  * (bias_gu [2I] fp32 in the same order, or NULL). I must be a multiple of 128. */
 FMKA_API int fmka_gemm_bf16_swiglu(const void* a, int64_t lda, const void* w_gu, int64_t ldw, const float* bias_gu,
                           void* c, int64_t ldc, int M, int I, int K, fmka_stream_t stream);
+
+/* RMSNorm of the decoder layers around the patched self_attn (no counterpart
+ * in the reference's own code: it is transformers' LlamaRMSNorm, which the
+ * patched models run): y[r, :] = bf16(w * bf16(x[r, :] * rsqrt(mean(x[r, :]^2)
+ * + eps))) for r < rows, with the mean in fp32 and the same two roundings as the
+ * module. x, y bf16 with row strides ldx, ldy (elements); w bf16 [D]; D a
+ * multiple of 8, at most 8192. */
+FMKA_API int fmka_rmsnorm_bf16(const void* x, int64_t ldx, const void* w, float eps, void* y, int64_t ldy, int rows,
+                               int D, fmka_stream_t stream);
 
 /* ------------------------------------------------ several GPUs of a box ---
  * The ranks of a sequence group (one process per GPU) share buffers through

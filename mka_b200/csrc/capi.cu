@@ -43,6 +43,8 @@ int launch_attn_prefill(const __nv_bfloat16* q, int64_t q_sb, int64_t q_sh, int6
                         int causal, float scale, cudaStream_t stream, const PeerPtrs* o_dst = nullptr,
                         int n_dst = 0, int rows_per_dst = 0);
 int launch_peer_barrier(uint32_t* const* flags, int rank, int n, uint32_t epoch, cudaStream_t stream);
+int launch_rmsnorm(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* w, float eps, __nv_bfloat16* y,
+                   int64_t ldy, int rows, int D, cudaStream_t stream);
 size_t attn_decode_workspace_bytes(int B, int Hq, int num_splits);
 int attn_decode_plan(int B, int Hkv, int Tk, int requested, int* keys_per_split_out);
 int launch_attn_decode(const __nv_bfloat16* q, int64_t q_sb, int64_t q_sh, const __nv_bfloat16* k,
@@ -444,6 +446,13 @@ int fmka_attn_fwd_prefill(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_s
     return set_error(kErrInvalidArgument, "attn_prefill: null pointer");
   return launch_attn_prefill(bf(q), q_sb, q_sh, q_st, bf(k), bf(v), kv_sb, kv_sh, kv_st, bfw(o), o_sb, o_st, o_sh,
                              lse, lse_sb, lse_sh, B, Hq, Hkv, Tq, Tk, head_dim, causal, scale, as_stream(stream));
+}
+
+int fmka_rmsnorm_bf16(const void* x, int64_t ldx, const void* w, float eps, void* y, int64_t ldy, int rows, int D,
+                      fmka_stream_t stream) {
+  if (x == nullptr || w == nullptr || y == nullptr) return set_error(kErrInvalidArgument, "rmsnorm: null pointer");
+  if (!std::isfinite(eps) || eps < 0.f) return set_error(kErrInvalidArgument, "rmsnorm: eps must be finite and >= 0");
+  return launch_rmsnorm(bf(x), ldx, bf(w), eps, bfw(y), ldy, rows, D, as_stream(stream));
 }
 
 int fmka_attn_fwd_prefill_scatter(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, const void* k,

@@ -453,6 +453,26 @@ def attn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Option
     return out, lse
 
 
+# ----------------------------------------------------- decoder-layer norm --
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """RMSNorm over the last dimension as transformers' LlamaRMSNorm computes it
+    for bf16 input: bf16(w * bf16(x * rsqrt(mean(x^2) + eps))), one pass."""
+    _check_cuda(x, weight)
+    _check_bf16(x, weight)
+    D = x.shape[-1]
+    if weight.shape != (D,) or not weight.is_contiguous():
+        raise RuntimeError("rmsnorm: weight must be a contiguous [D] tensor")
+    x2 = x.reshape(-1, D)
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    y2 = out.view(-1, D)
+    _lib.call("fmka_rmsnorm_bf16", x2.data_ptr(), x2.stride(0), weight.data_ptr(), float(eps), y2.data_ptr(),
+              y2.stride(0), x2.shape[0], D, _stream(x))
+    return out
+
+
 # ---------------------------------------- reference-compatible op wrappers --
 def has_fastmka_cuda() -> bool:
     """True when the library loads and a CUDA device is visible (mka/cuda/ops.py:25-26)."""

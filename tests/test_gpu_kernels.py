@@ -313,3 +313,30 @@ def test_gemm_kblocked(ops, nblk, M, kb, N):
     out = ops.gemm_kblocked(blocks, w, bias)
     a = blocks.permute(1, 0, 2).reshape(M, nblk * kb).float()
     assert _rel(out, a @ w.float().t() + bias) < 1e-2
+
+
+@pytest.mark.parametrize("rows,D", [(1, 4096), (300, 4096), (77, 1024), (5, 520), (3, 8192), (1000, 3584)])
+def test_rmsnorm_matches_transformers(ops, rows, D):
+    """The one-pass RMSNorm against transformers' LlamaRMSNorm on the same bf16
+    input and weight (same two roundings; the fp32 sum of squares runs in a
+    different order, so a few elements differ by a bf16 step or two) and against
+    an fp32 restatement."""
+    from transformers.models.llama.modeling_llama import LlamaRMSNorm
+
+    g = torch.Generator(device="cuda").manual_seed(rows + D)
+    x = (torch.randn(rows, D, device="cuda", generator=g) * 3).bfloat16()
+    norm = LlamaRMSNorm(D, eps=1e-5).cuda().to(torch.bfloat16)
+    with torch.no_grad():
+        norm.weight.copy_(1 + 0.1 * torch.randn(D, device="cuda", generator=g))
+        ref = norm(x)
+    y = ops.rmsnorm(x, norm.weight.detach(), 1e-5)
+    assert y.shape == x.shape and y.dtype == torch.bfloat16
+    diff = (y.float() - ref.float()).abs()
+    # a sum-order difference can move the first rounding by one step, which the
+    # product with the weight carries into y: allow a few bf16 steps, rarely
+    assert (diff <= ref.float().abs() * 2 ** -6 + 2 ** -14).all()
+    assert (diff == 0).float().mean().item() > 0.99
+    xf = x.float()
+    r32 = norm.weight.float() * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5))
+    assert _rel(y, r32) < 1e-2
+    assert ops.device_status() == 0

@@ -190,3 +190,24 @@ def test_l3_memory_reaches_every_patched_layer(monkeypatch):
     assert [s[0] for s in seen] == [0, 1]
     assert all(s[1] is r and s[2] for s in seen)
     assert all(layer.self_attn.use_l3 for layer in model.model.layers)
+
+
+def test_norm_fusion_walks_modules_and_keeps_parameter_names():
+    """Host logic only: every RMSNorm of a bf16 Llama (two per decoder layer and
+    the final one) is replaced, the state_dict is unchanged, a second call
+    changes nothing, fp32 models are left alone, and the fused module refuses
+    CPU input (it has no CPU path)."""
+    from mka_b200.hf.norm import FusedRMSNorm, apply_norm_fusion
+
+    model = _tiny_llama()
+    assert apply_norm_fusion(model) == 0  # fp32 weights: not installed
+    model = model.to(torch.bfloat16)
+    keys = {k: v.clone() for k, v in model.state_dict().items()}
+    assert apply_norm_fusion(model) == 2 * 2 + 1
+    assert isinstance(model.model.norm, FusedRMSNorm)
+    assert all(isinstance(layer.input_layernorm, FusedRMSNorm) for layer in model.model.layers)
+    after = model.state_dict()
+    assert set(after) == set(keys) and all(torch.equal(after[k], keys[k]) for k in keys)
+    assert apply_norm_fusion(model) == 0
+    with pytest.raises(RuntimeError, match="CUDA"):
+        model.model.norm(torch.zeros(2, 256, dtype=torch.bfloat16))
