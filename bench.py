@@ -646,8 +646,10 @@ def bench_model(args, device):
     N(0, 0.02)) with every self_attn replaced by the FastMKA module through the
     reference's patch API with three levels (L1 + L2 + L3; the L3 memory is one
     seeded N(0, 0.5) [1, 65536, 4096] tensor passed with the model call, which
-    transformers forwards to every self_attn), and with --model-mlp fused every
-    MLP by the fused SwiGLU MLP; one prefill forward of a 65536-token sequence
+    transformers forwards to every self_attn), every MLP's SiLU product by the
+    one-pass kernel (--model-mlp silu_mul; "fused" takes the SwiGLU GEMM,
+    "transformers" leaves the MLP alone) and every RMSNorm by the one-pass
+    kernel (--model-norm); one prefill forward of a 65536-token sequence
     per step (logits of the last position only). Also times one patched
     self_attn alone at that length, the part of each layer this package
     replaces."""
@@ -668,7 +670,8 @@ def bench_model(args, device):
             torch.manual_seed(5)
             model = LlamaForCausalLM(cfg).eval()
             patched = apply_hf_attention_patch(model, HFPatchConfig(use_l3=True, verbose=False))
-            fused_mlp = apply_mlp_fusion(model) if args.model_mlp == "fused" else 0
+            fused_mlp = (apply_mlp_fusion(model, mode="swiglu" if args.model_mlp == "fused" else "silu_mul")
+                         if args.model_mlp != "transformers" else 0)
             fused_norms = apply_norm_fusion(model) if args.model_norm == "fused" else 0
     finally:
         torch.set_default_dtype(prev)
@@ -708,8 +711,9 @@ def bench_model(args, device):
                    "heads": f"{c['H']}/{c['HKV']}", "vocab": c["vocab"], "rope_theta": c["theta"],
                    "batch": c["B"], "seq_len": c["T"], "logits": "last position",
                    "levels": "L1 + L2 + L3 (L3: seeded N(0, 0.5) memory [1, 65536, 4096], the same for every layer)",
-                   "mlp": ("gate/up GEMM with the SiLU-product epilogue, then down_proj (FusedSwiGLUMLP)"
-                           if fused_mlp else "transformers LlamaMLP (cuBLAS GEMMs + elementwise)"),
+                   "mlp": {"fused": "gate/up GEMM with the SiLU-product epilogue, then down_proj (FusedSwiGLUMLP)",
+                           "silu_mul": "transformers' cuBLAS GEMMs, one-pass SiLU product (SiLUMulMLP)",
+                           "transformers": "transformers LlamaMLP (cuBLAS GEMMs + elementwise)"}[args.model_mlp],
                    "norms": ("one-pass RMSNorm kernel (FusedRMSNorm)" if fused_norms
                              else "transformers LlamaRMSNorm (elementwise kernels)")},
         "data": "synthetic token ids U[0, vocab), random N(0, 0.02) bf16 weights",
@@ -791,8 +795,9 @@ def main():
     ap.add_argument("--no-long", action="store_true", help="skip the long-context (L3, seq 32768) measurement")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="how a head-sharded sequence group exchanges rows (long context, N > 2)")
-    ap.add_argument("--model-mlp", choices=["fused", "transformers"], default="transformers",
-                    help="the full-model line's MLP: transformers' own (default) or the fused SwiGLU GEMM")
+    ap.add_argument("--model-mlp", choices=["fused", "silu_mul", "transformers"], default="silu_mul",
+                    help="the full-model line's MLP: transformers' GEMMs with the one-pass SiLU product (default), "
+                         "transformers' own, or the fused SwiGLU GEMM")
     ap.add_argument("--model-norm", choices=["fused", "transformers"], default="fused",
                     help="the full-model line's RMSNorms: the one-pass kernel (default) or transformers' own")
     ap.add_argument("--no-model", action="store_true",

@@ -42,9 +42,10 @@
  *   fmka_gemm_bf16_swiglu   outside the attention path: the gate/up projections and
  *                           SiLU product of the Llama MLP around the patched
  *                           self_attn (transformers LlamaMLP), one GEMM
- *   fmka_rmsnorm_bf16       outside the attention path: the RMSNorm of the decoder
- *                           layers around the patched self_attn (transformers
- *                           LlamaRMSNorm / Qwen2RMSNorm), one pass
+ *   fmka_rmsnorm_bf16,      outside the attention path: the RMSNorm and the MLP's
+ *   fmka_silu_mul_bf16      SiLU product of the decoder layers around the patched
+ *                           self_attn (transformers LlamaRMSNorm / LlamaMLP), one
+ *                           pass each
  *   fmka_attn_fwd_prefill_scatter, fmka_gemm_bf16_kblocked_scatter, fmka_peer_*
  *                           the head-sharded layer over several GPUs of a box:
  *                           attention rows and o_proj rows stored straight into
@@ -259,6 +260,12 @@ FMKA_API int fmka_gemm_bf16_swiglu(const void* a, int64_t lda, const void* w_gu,
  * multiple of 8, at most 8192. */
 FMKA_API int fmka_rmsnorm_bf16(const void* x, int64_t ldx, const void* w, float eps, void* y, int64_t ldy, int rows,
                                int D, fmka_stream_t stream);
+
+/* SiLU product of the MLP around the patched self_attn (no counterpart in the
+ * reference's own code: transformers' LlamaMLP computes act_fn(gate) * up):
+ * out[i] = bf16(bf16(silu(g[i])) * u[i]) for n contiguous bf16 elements (n a
+ * multiple of 8); out may be g. */
+FMKA_API int fmka_silu_mul_bf16(const void* g, const void* u, void* out, int64_t n, fmka_stream_t stream);
 
 /* ------------------------------------------------ several GPUs of a box ---
  * The ranks of a sequence group (one process per GPU) share buffers through

@@ -55,6 +55,7 @@ _SIGNATURES = {
     "fmka_peer_close": (_I, [_P]),
     "fmka_peer_barrier": (_I, [_P, _I, _I, c_uint32, _P]),
     "fmka_rmsnorm_bf16": (_I, [_P, _L, _P, _F, _P, _L, _I, _I, _P]),
+    "fmka_silu_mul_bf16": (_I, [_P, _P, _P, _L, _P]),
     "fmka_attn_decode_num_splits": (_I, [_I, _I, _I]),
     "fmka_attn_decode_workspace_size": (c_size_t, [_I, _I, _I, _I, _I]),
     "fmka_attn_decode_splitkv": (_I, [_P, _L, _L, _P, _P, _L, _L, _L, _P, _L, _L, _P, _L,

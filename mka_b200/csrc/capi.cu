@@ -45,6 +45,8 @@ int launch_attn_prefill(const __nv_bfloat16* q, int64_t q_sb, int64_t q_sh, int6
 int launch_peer_barrier(uint32_t* const* flags, int rank, int n, uint32_t epoch, cudaStream_t stream);
 int launch_rmsnorm(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* w, float eps, __nv_bfloat16* y,
                    int64_t ldy, int rows, int D, cudaStream_t stream);
+int launch_silu_mul(const __nv_bfloat16* g, const __nv_bfloat16* u, __nv_bfloat16* out, int64_t n,
+                    cudaStream_t stream);
 size_t attn_decode_workspace_bytes(int B, int Hq, int num_splits);
 int attn_decode_plan(int B, int Hkv, int Tk, int requested, int* keys_per_split_out);
 int launch_attn_decode(const __nv_bfloat16* q, int64_t q_sb, int64_t q_sh, const __nv_bfloat16* k,
@@ -453,6 +455,11 @@ int fmka_rmsnorm_bf16(const void* x, int64_t ldx, const void* w, float eps, void
   if (x == nullptr || w == nullptr || y == nullptr) return set_error(kErrInvalidArgument, "rmsnorm: null pointer");
   if (!std::isfinite(eps) || eps < 0.f) return set_error(kErrInvalidArgument, "rmsnorm: eps must be finite and >= 0");
   return launch_rmsnorm(bf(x), ldx, bf(w), eps, bfw(y), ldy, rows, D, as_stream(stream));
+}
+
+int fmka_silu_mul_bf16(const void* g, const void* u, void* out, int64_t n, fmka_stream_t stream) {
+  if (g == nullptr || u == nullptr || out == nullptr) return set_error(kErrInvalidArgument, "silu_mul: null pointer");
+  return launch_silu_mul(bf(g), bf(u), bfw(out), n, as_stream(stream));
 }
 
 int fmka_attn_fwd_prefill_scatter(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, const void* k,

@@ -10,7 +10,8 @@ down_proj with the package's GEMM, so each layer's feed-forward reads x once
 and writes only the [tokens, I] product. Parameter names stay those of the
 wrapped module (gate_proj / up_proj / down_proj), so state_dicts load
 unchanged. `apply_mlp_fusion` installs it in every decoder layer whose MLP has
-that form.
+that form. `SiLUMulMLP` keeps transformers' three GEMMs and only fuses the
+activation and the product into one pass (`apply_mlp_fusion(mode="silu_mul")`).
 """
 from __future__ import annotations
 
@@ -70,19 +71,52 @@ class FusedSwiGLUMLP(nn.Module):
         return out.view(*shape[:-1], out.shape[-1]).to(x.dtype)
 
 
-def apply_mlp_fusion(model: nn.Module, verbose: bool = False) -> int:
-    """Replaces every decoder layer's gated SiLU MLP with FusedSwiGLUMLP;
-    returns the number of layers changed (inference: no autograd through it)."""
+class SiLUMulMLP(nn.Module):
+    """Drop-in for a gated SiLU MLP that keeps its three GEMMs (the wrapped
+    Linears, cuBLAS through torch) and replaces act_fn(gate) * up, two
+    elementwise kernels over the [tokens, I] intermediates, by one pass
+    (ops.silu_mul, written over the gate output). Same parameter names."""
+
+    def __init__(self, mlp: nn.Module):
+        super().__init__()
+        self.gate_proj = mlp.gate_proj
+        self.up_proj = mlp.up_proj
+        self.down_proj = mlp.down_proj
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        g = self.gate_proj(x)
+        u = self.up_proj(x)
+        if g.dtype != torch.bfloat16:
+            raise RuntimeError("SiLUMulMLP needs a bf16 model")
+        with torch.no_grad():
+            h = ops.silu_mul(g.contiguous(), u.contiguous(), out=g if g.is_contiguous() else None)
+        return self.down_proj(h)
+
+
+def apply_mlp_fusion(model: nn.Module, verbose: bool = False, mode: str = "swiglu") -> int:
+    """Replaces every decoder layer's gated SiLU MLP, with FusedSwiGLUMLP (mode
+    "swiglu": gate/up GEMM with the SiLU-product epilogue) or SiLUMulMLP (mode
+    "silu_mul": transformers' GEMMs, one-pass SiLU product); returns the number
+    of layers changed (inference: no autograd through it)."""
+    if mode not in ("swiglu", "silu_mul"):
+        raise ValueError("mode must be 'swiglu' or 'silu_mul'")
     fused = 0
     for layer in _iter_layers(model):
         mlp = getattr(layer, "mlp", None)
-        if mlp is None or isinstance(mlp, FusedSwiGLUMLP):
+        if mlp is None or isinstance(mlp, (FusedSwiGLUMLP, SiLUMulMLP)):
             continue
         if not all(hasattr(mlp, n) for n in ("gate_proj", "up_proj", "down_proj")):
             continue
-        if not _is_silu(getattr(mlp, "act_fn", None)) or mlp.gate_proj.out_features % 128:
+        if not _is_silu(getattr(mlp, "act_fn", None)):
             continue
-        layer.mlp = FusedSwiGLUMLP(mlp)
+        if mode == "swiglu":
+            if mlp.gate_proj.out_features % 128:
+                continue
+            layer.mlp = FusedSwiGLUMLP(mlp)
+        else:
+            if mlp.gate_proj.weight.dtype != torch.bfloat16 or mlp.gate_proj.out_features % 8:
+                continue
+            layer.mlp = SiLUMulMLP(mlp)
         fused += 1
     if verbose:
         print(f"[MKA patch] fused MLP layers: {fused}")

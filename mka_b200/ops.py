@@ -473,6 +473,21 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: Optional[tor
     return out
 
 
+def silu_mul(g: torch.Tensor, u: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """bf16(bf16(silu(g)) * u), the SiLU product of a gated MLP, in one pass
+    (out may be g)."""
+    _check_cuda(g, u)
+    _check_bf16(g, u)
+    if g.shape != u.shape or not g.is_contiguous() or not u.is_contiguous():
+        raise RuntimeError("silu_mul: g and u must be contiguous tensors of the same shape")
+    if out is None:
+        out = torch.empty_like(g)
+    elif out.shape != g.shape or not out.is_contiguous() or out.dtype != torch.bfloat16:
+        raise RuntimeError("silu_mul: out must be a contiguous bf16 tensor of g's shape")
+    _lib.call("fmka_silu_mul_bf16", g.data_ptr(), u.data_ptr(), out.data_ptr(), g.numel(), _stream(g))
+    return out
+
+
 # ---------------------------------------- reference-compatible op wrappers --
 def has_fastmka_cuda() -> bool:
     """True when the library loads and a CUDA device is visible (mka/cuda/ops.py:25-26)."""

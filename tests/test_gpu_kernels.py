@@ -340,3 +340,30 @@ def test_rmsnorm_matches_transformers(ops, rows, D):
     r32 = norm.weight.float() * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5))
     assert _rel(y, r32) < 1e-2
     assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("shape,inplace", [((96, 512), False), ((3, 1000, 344), True), ((8,), False),
+                                           ((257, 14336), True)])
+def test_silu_mul_matches_transformers(ops, shape, inplace):
+    """bf16(bf16(silu(g)) * u) in one pass against torch's act_fn(gate) * up on
+    the same bf16 tensors (two kernels, same roundings; the exponential may
+    differ by an fp32 ulp, which can move a rare element by one bf16 step), and
+    against an fp32 restatement. inplace: the product overwrites g."""
+    n = 1
+    for s in shape:
+        n *= s
+    g = torch.Generator(device="cuda").manual_seed(n)
+    gt = (torch.randn(*shape, device="cuda", generator=g) * 4).bfloat16()
+    ut = (torch.randn(*shape, device="cuda", generator=g) * 2).bfloat16()
+    ref = torch.nn.functional.silu(gt) * ut
+    r32 = torch.nn.functional.silu(gt.float()) * ut.float()
+    gin = gt.clone()
+    y = ops.silu_mul(gin, ut, out=gin if inplace else None)
+    if inplace:
+        assert y.data_ptr() == gin.data_ptr()
+    assert y.shape == gt.shape and y.dtype == torch.bfloat16
+    diff = (y.float() - ref.float()).abs()
+    assert (diff <= ref.float().abs() * 2 ** -7 + 2 ** -30).all()
+    assert (diff == 0).float().mean().item() > 0.99
+    assert _rel(y, r32) < 1e-2
+    assert ops.device_status() == 0

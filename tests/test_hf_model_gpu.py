@@ -137,6 +137,55 @@ def test_mlp_fusion_walks_layers_and_keeps_parameter_names():
     assert apply_mlp_fusion(model) == 0
 
 
+def test_silu_mul_mlp_walk_keeps_parameter_names():
+    """Host logic of mode="silu_mul": bf16 gated SiLU MLPs are replaced by
+    SiLUMulMLP with the same state_dict; an fp32 model is left alone."""
+    from mka_b200.hf.mlp import SiLUMulMLP, apply_mlp_fusion
+
+    model = _tiny_llama()
+    assert apply_mlp_fusion(model, mode="silu_mul") == 0  # fp32 weights: not replaced
+    model = model.to(torch.bfloat16)
+    keys = {k: v.clone() for k, v in model.state_dict().items()}
+    assert apply_mlp_fusion(model, mode="silu_mul") == 2
+    assert all(isinstance(layer.mlp, SiLUMulMLP) for layer in model.model.layers)
+    after = model.state_dict()
+    assert set(after) == set(keys)
+    assert all(torch.equal(after[k], keys[k]) for k in keys)
+    assert apply_mlp_fusion(model, mode="silu_mul") == 0
+    assert apply_mlp_fusion(model) == 0
+    with pytest.raises(ValueError):
+        apply_mlp_fusion(model, mode="gelu")
+
+
+@pytest.mark.gpu
+def test_silu_mul_mlp_matches_transformers_mlp():
+    """SiLUMulMLP against transformers' LlamaMLP (same GEMMs, same roundings)
+    and against an fp32 SwiGLU MLP; a patched model with it against the same
+    model with transformers' MLP."""
+    from mka_b200.hf.mlp import SiLUMulMLP, apply_mlp_fusion
+
+    model = _tiny_llama().to(torch.bfloat16)
+    assert apply_hf_attention_patch(model, HFPatchConfig(verbose=False)) == 2
+    model = model.to("cuda")
+    fused = copy.deepcopy(model)
+    assert apply_mlp_fusion(fused, mode="silu_mul") == 2
+    g = torch.Generator().manual_seed(5)
+    x = (torch.randn(2, 96, 256, generator=g) * 0.5).bfloat16().cuda()
+    with torch.no_grad():
+        mlp = model.model.layers[0].mlp
+        sm = SiLUMulMLP(mlp)
+        f32 = lambda lin: lin.weight.detach().float().cpu()  # noqa: E731
+        xf = x.float().cpu()
+        ref = torch.nn.functional.silu(xf @ f32(mlp.gate_proj).T) * (xf @ f32(mlp.up_proj).T)
+        ref = ref @ f32(mlp.down_proj).T
+        assert _rel(sm(x), ref) < 2e-2
+        assert _rel(sm(x), mlp(x)) < 1e-2
+        ids = torch.randint(0, 128, (2, 96), generator=g).cuda()
+        a = model(ids).logits
+        b = fused(ids).logits
+    assert _rel(b, a) < 1e-2
+
+
 @pytest.mark.gpu
 def test_fused_mlp_matches_transformers_mlp():
     """The fused MLP of one layer against an fp32 SwiGLU MLP on the CPU, and a
