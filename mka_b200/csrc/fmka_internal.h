@@ -29,10 +29,13 @@ int set_error(int code, const std::string& msg);
 int check_cuda(cudaError_t e, const char* what);
 
 // ------------------------------------------------------------- tensor maps --
-// Encodes a rank-2 or rank-3 bf16 tiled tensor map with 128-byte swizzle.
+// Encodes a bf16 tiled tensor map (rank 2 to 5), with or without 128-byte swizzle.
 // dims/strides are innermost first; strides are in bytes for dims 1..rank-1.
 int make_tmap_bf16(CUtensorMap* out, const void* base, int rank, const uint64_t* dims,
                    const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128);
+// The same for fp32 elements, without swizzle.
+int make_tmap_f32(CUtensorMap* out, const void* base, int rank, const uint64_t* dims,
+                  const uint64_t* strides_bytes, const uint32_t* box);
 
 // ------------------------------------------------------------ peer memory --
 // Most ranks (GPUs of one box) that exchange data through peer mappings.

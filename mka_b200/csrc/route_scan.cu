@@ -31,18 +31,20 @@
 // scan continues with a zero contribution. Three CTAs share an SM so that one
 // CTA's waits are covered by the others' loads.
 //
-// Two kernels. route_ema_blend_kernel covers every mode (H or K/V output, a
-// given L2, a carried EMA state, long memory). kv_scan_kernel is the layer's
-// case (K/V output, short memory, no carried state) with the mode fixed at
-// compile time and the state scaled by 1 / (1 - beta), one FMA per step.
+// Three kernels. route_ema_blend_kernel covers every mode (H or K/V output, a
+// given L2, a carried EMA state, long memory). kv_window_kernel is the layer's
+// case (K/V output, short memory, no carried state): a streaming kernel with
+// no communication between CTAs (each CTA recomputes the state entering its
+// token segment from a warm-up window). kv_scan_kernel is the same case in the
+// chunk-parallel look-back form, kept for tensors that do not suit TMA.
 // Measured on the layer's K/V-mode scan (batch 4 x 8192 tokens, 1024
-// channels): 0.121 ms with a [32][8] shared-memory layout, whose eight-way bank
-// conflicts kept the L1 pipe 74 % busy; 0.071-0.074 ms for the general kernel
-// with the float4 planes; 0.058 ms for kv_scan_kernel (0.060 at 16 warps x
-// 128-token chunks, 2 CTAs per SM), 0.057 ms with the RoPE rows prefetched
-// into L1 before the look-back.
+// channels, device time): 0.121 ms with a [32][8] shared-memory layout, whose
+// eight-way bank conflicts kept the L1 pipe 74 % busy; 0.071-0.074 ms for the
+// general kernel with the float4 planes; 0.057 ms for kv_scan_kernel; 0.040 ms
+// for kv_window_kernel.
 #include <cstdlib>
 #include <mutex>
+#include <type_traits>
 
 #include "fmka_internal.h"
 #include "ptx.cuh"
@@ -115,6 +117,12 @@ struct ScanParams {
   float* inc;              // [nseq * nchunks * kSlice]
   int nds, nchunks;
   uint32_t* status;
+  // kv_window_kernel: tokens of the warm-up window; the CTAs of slices with K
+  // heads (ds < nds_k, the first n_ctas_k CTAs) and of V-only slices have their
+  // own segment lengths; whether the L3 / RoPE tensor maps have a batch dimension
+  int win_tokens, seg_len_k, seg_len_v, nds_k, n_ctas_k;
+  int l3_bcast, rope_bcast;
+  float beta4, beta32;
 };
 
 __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
@@ -755,6 +763,408 @@ __global__ void __launch_bounds__(kThreads, FMKA_SCAN_MINB) kv_scan_kernel(const
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// The layer's stage 1 as a streaming kernel: no communication between CTAs.
+//
+// With short memory (beta^W < 2^-40 for a window of W tokens) the state
+// entering token s is, to within 2^-40 of its newest term, the zero-state scan
+// of the W tokens before s. So each CTA owns a segment of tokens of one
+// (batch row, 256-channel slice), first scans the W tokens before the segment
+// (warm-up: loads and FMAs only) and then streams the segment, carrying the
+// state from sub-chunk to sub-chunk. There is no look-back, no ticket and no
+// flag memory; the grid is one CTA per SM.
+//
+// Warp roles: warp 8 drives a ring of shared-memory stages with TMA (per
+// 32-token sub-chunk: the y tile [32 x 256] bf16, and in the segment proper the
+// y3 tile and the RoPE cos / sin rows [32 x 128] fp32) and writes the gate of
+// the sub-chunk's 32 tokens into the stage, from router logits it loaded one
+// ring length earlier (lane i: token i); warps 0-7 take 4 tokens each. A lane
+// holds channels 4q..4q+3 and 64+4q..64+4q+3 of one head (q = lane % 16, head
+// = lane / 16 within the slice), so the rotate-half partner of every channel is
+// in the same lane and the RoPE needs no shuffle. Per sub-chunk a warp scans its
+// 4 tokens from a zero state, publishes the aggregate, and after one named
+// barrier finds its incoming state from the carried state and the aggregates of
+// the warps before it; warp 7 carries the state to the next sub-chunk. The
+// state is kept in u units (u_t = beta u_{t-1} + y_t, EMA = (1 - beta) u).
+// During the warm-up each warp keeps its own running sum of its aggregates
+// (A_w = beta^32 A_w + a_w), which needs no barrier; the state at the segment
+// start is sum_w beta^(4 (7 - w)) A_w.
+constexpr int kWinTok = 32;                              // tokens per sub-chunk
+constexpr int kWinWarps = 8;                             // consumer warps
+constexpr int kWinTpw = kWinTok / kWinWarps;             // tokens per consumer warp (4)
+constexpr int kWinThreads = (kWinWarps + 1) * 32;
+constexpr int kWinRowBytes = kSlice * 2;                 // one token's 256 channels, bf16
+constexpr int kWinYBytes = kWinTok * kWinRowBytes;       // 16 KB
+constexpr int kWinRopeBytes = kWinTok * 128 * 4;         // 16 KB for cos, 16 KB for sin
+constexpr int kWinGateBytes = kWinTok * 16;             // float4 gate per token
+constexpr int kWinSmemBudget = 200 * 1024;
+#ifndef FMKA_WIN_WARM_MULTI
+#define FMKA_WIN_WARM_MULTI 1
+#endif
+
+template <bool kRope, bool kL3>
+struct WinLayout {
+  static constexpr int y = 0;
+  static constexpr int y3 = kWinYBytes;
+  static constexpr int cs = y3 + (kL3 ? kWinYBytes : 0);
+  static constexpr int sn = cs + (kRope ? kWinRopeBytes : 0);
+  static constexpr int gate = sn + (kRope ? kWinRopeBytes : 0);
+  static constexpr int stage = gate + kWinGateBytes;
+  static constexpr int fit = kWinSmemBudget / stage;
+  static constexpr int stages = fit > 8 ? 8 : fit;
+  static constexpr int bytes = stages * stage;
+  // the warm-up needs only y: a stage then holds this many 32-token y tiles
+  static constexpr int warm_tiles = FMKA_WIN_WARM_MULTI ? gate / kWinYBytes : 1;
+};
+
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// 4 bf16 at channels c..c+3 and 4 at c+64..c+67 -> 8 floats (lo then hi)
+__device__ __forceinline__ void unpack_lohi(const uint2& lo, const uint2& hi, float (&f)[8]) {
+  f[0] = bf16lo_to_f32(lo.x);
+  f[1] = bf16hi_to_f32(lo.x);
+  f[2] = bf16lo_to_f32(lo.y);
+  f[3] = bf16hi_to_f32(lo.y);
+  f[4] = bf16lo_to_f32(hi.x);
+  f[5] = bf16hi_to_f32(hi.x);
+  f[6] = bf16lo_to_f32(hi.y);
+  f[7] = bf16hi_to_f32(hi.y);
+}
+
+template <bool kRope, bool kBias, bool kL3>
+__global__ void __launch_bounds__(kWinThreads, 1)
+    kv_window_kernel(const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmY3,
+                     const __grid_constant__ CUtensorMap tmCos, const __grid_constant__ CUtensorMap tmSin,
+                     const __grid_constant__ ScanParams p) {
+  using Lay = WinLayout<kRope, kL3>;
+  constexpr int S = Lay::stages;
+  extern __shared__ __align__(1024) uint8_t win_smem[];
+  __shared__ __align__(8) uint64_t full_bar[S];
+  __shared__ __align__(8) uint64_t empty_bar[S];
+  __shared__ float4 s_agg[2][kWinWarps][2][32];  // per warp: zero-state aggregate of its 4 tokens
+  __shared__ float4 s_carry[2][2][32];           // state after the previous sub-chunk
+  __shared__ float4 s_wa[kWinWarps][2][32];      // warm-up sums A_w
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  // CTA -> (segment, batch row, slice); neighbouring CTAs share a token range.
+  // The CTAs of K slices (RoPE) come first, with their own segment length.
+  const bool kgrp = static_cast<int>(blockIdx.x) < p.n_ctas_k;
+  const int nds_g = kgrp ? p.nds_k : p.nds - p.nds_k;
+  const int bid = kgrp ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x) - p.n_ctas_k;
+  const int nss = p.B * nds_g;
+  const int seg = bid / nss;
+  const int ss = bid % nss;
+  const int b = ss / nds_g;
+  const int ds = (kgrp ? 0 : p.nds_k) + ss % nds_g;
+  const int T = p.T;
+  const int seg_len = kgrp ? p.seg_len_k : p.seg_len_v;
+  const int s0 = seg * seg_len;
+  const int s1 = min(s0 + seg_len, T);
+  const int ws = max(0, s0 - p.win_tokens);
+  const int nwarm = (s0 - ws) / kWinTok;                             // warm-up sub-chunks
+  constexpr int kWT = Lay::warm_tiles;
+  const int nwst = (nwarm + kWT - 1) / kWT;                          // warm-up stages
+  const int nsub = nwst + (s1 - s0 + kWinTok - 1) / kWinTok;          // stage uses
+  const int nk = p.D >> 1;
+  const bool cta_has_k = ds * kSlice < nk;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full_bar[i], 2);  // the producer's expect_tx arrival and its arrival after the gates
+      mbar_init(&empty_bar[i], kWinWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kWinWarps) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmY);
+      if (kL3) tma_prefetch_desc(&tmY3);
+      if (kRope && cta_has_k) {
+        tma_prefetch_desc(&tmCos);
+        tma_prefetch_desc(&tmSin);
+      }
+    }
+    const uint32_t main_tx =
+        kWinYBytes + (kL3 ? kWinYBytes : 0) + ((kRope && cta_has_k) ? 2 * kWinRopeBytes : 0);
+    const int b3 = p.l3_bcast ? 0 : b;
+    const int rb = p.rope_bcast ? 0 : b;
+    bool dead = false;
+    // router logits of token (segment sub-chunk m) * 32 + lane, loaded S stage uses ahead
+    const float b20 = p.b2 ? p.b2[0] : 0.f, b21 = p.b2 ? p.b2[1] : 0.f, b22 = (kL3 && p.b2) ? p.b2[2] : 0.f;
+    auto load_logits = [&](int m, float (&lg)[3]) {
+      const int t = s0 + m * kWinTok + lane;
+      lg[0] = lg[1] = 0.f;
+      lg[2] = -INFINITY;
+      if (m >= 0 && t < s1) {
+        const float* src = p.logits + ((int64_t)b * T + t) * p.L;
+        lg[0] = __ldg(src);
+        lg[1] = __ldg(src + 1);
+        if (kL3) lg[2] = __ldg(src + 2);
+      }
+    };
+    float lgq[S][3];
+#pragma unroll
+    for (int a = 0; a < S; ++a) load_logits(a - nwst, lgq[a]);
+    int st = 0;
+    uint32_t phase = 0;  // parity of this use of stage st; the previous use had phase ^ 1
+    for (int k = 0; k < nsub; ++k) {
+      if (k >= S && !dead) dead = !mbar_wait(&empty_bar[st], phase ^ 1u, p.status);
+      uint8_t* stage = win_smem + st * Lay::stage;
+      const bool in_seg = k >= nwst;
+      if (lane == 0 && !in_seg) {
+        const int tile0 = k * kWT;
+        const int ntile = min(kWT, nwarm - tile0);
+        mbar_arrive_expect_tx(&full_bar[st], static_cast<uint32_t>(ntile * kWinYBytes));
+        for (int i = 0; i < ntile; ++i)
+          tma_load_3d(stage + i * kWinYBytes, &tmY, &full_bar[st], ds * kSlice, ws + (tile0 + i) * kWinTok, b);
+      }
+      const int t0 = s0 + (k - nwst) * kWinTok;
+      if (lane == 0 && in_seg) {
+        mbar_arrive_expect_tx(&full_bar[st], main_tx);
+        tma_load_3d(stage + Lay::y, &tmY, &full_bar[st], ds * kSlice, t0, b);
+        if (kL3) tma_load_3d(stage + Lay::y3, &tmY3, &full_bar[st], ds * kSlice, min(t0, p.T3 - 1), b3);
+        if (kRope && cta_has_k) {
+          tma_load_3d(stage + Lay::cs, &tmCos, &full_bar[st], 0, t0, rb);
+          tma_load_3d(stage + Lay::sn, &tmSin, &full_bar[st], 0, t0, rb);
+        }
+      }
+      if (in_seg) {
+        // gate of token t0 + lane: lam0, lam1 (1 - beta), lam2
+        const int t = t0 + lane;
+        float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t < s1) {
+          float a0 = lgq[0][0] + b20, a1 = lgq[0][1] + b21, a2 = kL3 ? lgq[0][2] + b22 : -INFINITY;
+          const float mx = fmaxf(fmaxf(a0, a1), a2);
+          a0 = __expf(a0 - mx);
+          a1 = __expf(a1 - mx);
+          a2 = kL3 ? __expf(a2 - mx) : 0.f;
+          const float inv = 1.f / (a0 + a1 + a2);
+          a0 *= inv;
+          a1 *= inv;
+          a2 *= inv;
+          if (p.lam != nullptr && ds == 0) {
+            float* dstl = p.lam + ((int64_t)b * T + t) * p.L;
+            dstl[0] = a0;
+            dstl[1] = a1;
+            if (kL3) dstl[2] = a2;
+          }
+          g = make_float4(a0, a1 * p.one_minus_beta, a2, 0.f);
+        }
+        reinterpret_cast<float4*>(stage + Lay::gate)[lane] = g;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full_bar[st]);
+      // shift the logits queue by one stage use
+#pragma unroll
+      for (int a = 0; a + 1 < S; ++a) {
+#pragma unroll
+        for (int i = 0; i < 3; ++i) lgq[a][i] = lgq[a + 1][i];
+      }
+      load_logits(k + S - nwst, lgq[S - 1]);
+      if (++st == S) {
+        st = 0;
+        phase ^= 1u;
+      }
+    }
+    // no load may still be in flight when the CTA exits
+    for (int k = max(0, nsub - S); k < nsub; ++k)
+      if (!dead) dead = !mbar_wait(&full_bar[k % S], static_cast<uint32_t>(k / S) & 1u, p.status);
+    return;
+  }
+
+  // ------------------------------ consumers -------------------------------
+  const int hh = lane >> 4;
+  const int q = lane & 15;
+  const int col = hh * 128 + 4 * q;  // this lane's first channel in the slice (the second block is col + 64)
+  const int ch = ds * kSlice + col;
+  const bool is_k = ch < nk;
+  const int head = (is_k ? ch : ch - nk) >> 7;
+  __nv_bfloat16* out = (is_k ? p.kv_k : p.kv_v) + (int64_t)b * p.kv_sb + (int64_t)head * p.kv_sh +
+                       (int64_t)p.t_offset * p.kv_st + 4 * q;
+  float bias[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (kBias) {
+    const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.kv_bias + ch));
+    const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.kv_bias + ch + 64));
+    bias[0] = b0.x; bias[1] = b0.y; bias[2] = b0.z; bias[3] = b0.w;
+    bias[4] = b1.x; bias[5] = b1.y; bias[6] = b1.z; bias[7] = b1.w;
+  }
+  const float beta = p.beta;
+  const float b4 = p.beta4;
+  const float pw[kWinTpw] = {beta, beta * beta, beta * beta * beta, b4};
+  const int r0 = warp * kWinTpw;  // this warp's first row of a sub-chunk
+  bool dead = false;
+
+  // warm-up: this warp's running sum of its aggregates
+  float A[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  int st = 0;          // stage of sub-chunk k
+  uint32_t phase = 0;  // parity of its use of that stage
+  auto next_stage = [&]() {
+    if (++st == S) {
+      st = 0;
+      phase ^= 1u;
+    }
+  };
+  int k = 0;
+  for (; k < nwst; ++k, next_stage()) {
+    if (!dead) dead = !mbar_wait(&full_bar[st], phase, p.status);
+    const int ntile = min(kWT, nwarm - k * kWT);
+    const uint8_t* yb = win_smem + st * Lay::stage + r0 * kWinRowBytes + col * 2;
+    uint2 lo[kWT][kWinTpw], hi[kWT][kWinTpw];
+#pragma unroll
+    for (int i = 0; i < kWT; ++i) {
+      if (i < ntile) {
+#pragma unroll
+        for (int j = 0; j < kWinTpw; ++j) {
+          lo[i][j] = *reinterpret_cast<const uint2*>(yb + i * kWinYBytes + j * kWinRowBytes);
+          hi[i][j] = *reinterpret_cast<const uint2*>(yb + i * kWinYBytes + j * kWinRowBytes + 128);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[st]);
+#pragma unroll
+    for (int i = 0; i < kWT; ++i) {
+      if (i < ntile) {
+        float a[8];
+#pragma unroll
+        for (int j = 0; j < kWinTpw; ++j) {
+          float yf[8];
+          unpack_lohi(lo[i][j], hi[i][j], yf);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) a[c] = j == 0 ? yf[c] : fmaf(beta, a[c], yf[c]);
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c) A[c] = fmaf(p.beta32, A[c], a[c]);
+      }
+    }
+  }
+  put8(s_wa[warp], lane, A);  // read after the first barrier of the segment
+
+  // RoPE in this CTA: 0 none (V slice), 1 every lane (K slice), 2 the lanes of K heads
+  const int rope_mode = !kRope ? 0 : (!cta_has_k ? 0 : (ds * kSlice + kSlice <= nk ? 1 : 2));
+
+  // the segment
+  for (int km = 0; k < nsub; ++k, ++km, next_stage()) {
+    if (!dead) dead = !mbar_wait(&full_bar[st], phase, p.status);
+    const uint8_t* sb = win_smem + st * Lay::stage;
+    const int t0 = s0 + km * kWinTok;
+    float yf[kWinTpw][8];
+    float u[kWinTpw][8];
+#pragma unroll
+    for (int j = 0; j < kWinTpw; ++j) {
+      const uint8_t* row = sb + Lay::y + (r0 + j) * kWinRowBytes + col * 2;
+      unpack_lohi(*reinterpret_cast<const uint2*>(row), *reinterpret_cast<const uint2*>(row + 128), yf[j]);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) u[j][c] = j == 0 ? yf[j][c] : fmaf(beta, u[j - 1][c], yf[j][c]);
+    }
+    const int par = km & 1;
+    put8(s_agg[par][warp], lane, u[kWinTpw - 1]);
+    named_bar_sync(1, kWinWarps * 32);
+
+    // state entering this warp's first token
+    float s[8];
+    if (km == 0) {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) s[c] = 0.f;
+#pragma unroll
+      for (int v = 0; v < kWinWarps; ++v) {
+        float a[8];
+        get8(s_wa[v], lane, a);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) s[c] = fmaf(b4, s[c], a[c]);
+      }
+    } else {
+      get8(s_carry[par], lane, s);
+    }
+    for (int v = 0; v < warp; ++v) {
+      float a[8];
+      get8(s_agg[par][v], lane, a);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) s[c] = fmaf(b4, s[c], a[c]);
+    }
+    if (warp == kWinWarps - 1) {
+      float cnext[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) cnext[c] = fmaf(b4, s[c], u[kWinTpw - 1][c]);
+      put8(s_carry[par ^ 1], lane, cnext);
+    }
+
+    // blend, bias, RoPE, head-split store (RoPE mode fixed per CTA at compile time)
+    __nv_bfloat16* dst0 = out + (int64_t)(t0 + r0) * p.kv_st;
+    auto blend = [&](auto rope_c) {
+      constexpr int rm = decltype(rope_c)::value;
+#pragma unroll
+    for (int j = 0; j < kWinTpw; ++j) {
+      const int t = t0 + r0 + j;
+      const float4 g = reinterpret_cast<const float4*>(sb + Lay::gate)[r0 + j];
+      float o[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float uc = fmaf(pw[j], s[c], u[j][c]);
+        o[c] = fmaf(g.y, uc, fmaf(g.x, yf[j][c], bias[c]));
+      }
+      if (kL3) {
+        const int r3 = min(t, p.T3 - 1) - min(t0, p.T3 - 1);
+        const uint8_t* row3 = sb + Lay::y3 + r3 * kWinRowBytes + col * 2;
+        float y3f[8];
+        unpack_lohi(*reinterpret_cast<const uint2*>(row3), *reinterpret_cast<const uint2*>(row3 + 128), y3f);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) o[c] = fmaf(g.z, y3f[c], o[c]);
+      }
+      if (kRope && (rm == 1 || (rm == 2 && is_k))) {
+        const float* cr = reinterpret_cast<const float*>(sb + Lay::cs) + (r0 + j) * 128 + 4 * q;
+        const float* sr = reinterpret_cast<const float*>(sb + Lay::sn) + (r0 + j) * 128 + 4 * q;
+        const float4 cl = *reinterpret_cast<const float4*>(cr);
+        const float4 chv = *reinterpret_cast<const float4*>(cr + 64);
+        const float4 sl = *reinterpret_cast<const float4*>(sr);
+        const float4 shv = *reinterpret_cast<const float4*>(sr + 64);
+        const float cla[4] = {cl.x, cl.y, cl.z, cl.w}, cha[4] = {chv.x, chv.y, chv.z, chv.w};
+        const float sla[4] = {sl.x, sl.y, sl.z, sl.w}, sha[4] = {shv.x, shv.y, shv.z, shv.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float lo = o[c], hi = o[c + 4];
+          o[c] = fmaf(-hi, sla[c], lo * cla[c]);      // x1 cos - x2 sin
+          o[c + 4] = fmaf(lo, sha[c], hi * cha[c]);   // x2 cos + x1 sin
+        }
+      }
+      if (t < s1) {
+        __nv_bfloat16* dst = dst0 + (int64_t)j * p.kv_st;
+        *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+        *reinterpret_cast<uint2*>(dst + 64) = make_uint2(pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+      }
+    }
+    };
+    if (rope_mode == 1)
+      blend(std::integral_constant<int, 1>{});
+    else if (rope_mode == 0)
+      blend(std::integral_constant<int, 0>{});
+    else
+      blend(std::integral_constant<int, 2>{});
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[st]);
+  }
+}
+
+template <bool kRope, bool kBias, bool kL3>
+int launch_kv_window_t(const CUtensorMap& tmY, const CUtensorMap& tmY3, const CUtensorMap& tmCos,
+                       const CUtensorMap& tmSin, const ScanParams& p, int grid, cudaStream_t stream) {
+  constexpr int smem = WinLayout<kRope, kL3>::bytes;
+  auto kern = kv_window_kernel<kRope, kBias, kL3>;
+  int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                      "kv_window attr");
+  if (rc) return rc;
+  kern<<<grid, kWinThreads, smem, stream>>>(tmY, tmY3, tmCos, tmSin, p);
+  return check_cuda(cudaGetLastError(), "kv_window launch");
+}
+
 }  // namespace
 
 // FMKA_SCAN_GENERAL=1 sends the layer's K/V scan to the general kernel too
@@ -765,6 +1175,132 @@ static bool scan_general_forced() {
     return e != nullptr && e[0] == '1';
   }();
   return on;
+}
+
+// FMKA_SCAN_WINDOW=0 keeps the layer's K/V scan on kv_scan_kernel (the
+// chunk-parallel look-back form) instead of kv_window_kernel.
+static bool scan_window_off() {
+  static const bool off = [] {
+    const char* e = std::getenv("FMKA_SCAN_WINDOW");
+    return e != nullptr && e[0] == '0';
+  }();
+  return off;
+}
+
+// Cost of a V-slice token relative to a K-slice token (RoPE) in kv_window_kernel,
+// used to split the grid between the two; FMKA_WIN_V_COST overrides it.
+static double win_v_cost() {
+  static const double c = [] {
+    const char* e = std::getenv("FMKA_WIN_V_COST");
+    const double v = e ? std::atof(e) : 0.0;
+    return v > 0.05 && v <= 4.0 ? v : 0.9;  // measured best of 0.5-1.05 at batch 2 and 4 x 8192
+  }();
+  return c;
+}
+
+// Window of kv_window_kernel: the fewest whole sub-chunks W (at most 64) with
+// |beta|^W < 2^-40; 0 when the memory is longer than that.
+static int window_tokens(float beta) {
+  const double bc = std::fabs(__builtin_powi((double)beta, kWinTok));
+  double w = 1.0;
+  for (int k = 1; k <= 64; ++k) {
+    w *= bc;
+    if (w < 0x1p-40) return k * kWinTok;
+  }
+  return 0;
+}
+
+// The layer's K/V scan through kv_window_kernel; returns -1 (nothing launched)
+// when a tensor does not suit TMA, so that the caller takes another kernel.
+static int launch_kv_window(ScanParams p, cudaStream_t stream) {
+  const int W = window_tokens(p.beta);
+  if (W == 0 || p.D % kSlice != 0 || scan_window_off()) return -1;
+  const bool rope = p.rope_cos != nullptr, bias = p.kv_bias != nullptr, l3v = p.l3 != nullptr;
+  auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  if (rope && ((p.rope_st % 4) || (p.rope_sb % 4) || !al16(p.rope_cos) || !al16(p.rope_sin))) return -1;
+  if (bias && !al16(p.kv_bias)) return -1;
+  if (p.x_st < p.D || (l3v && p.l3_st < p.D)) return -1;
+  CUtensorMap tmY, tmY3, tmCos, tmSin;
+  {
+    const uint64_t dims[3] = {(uint64_t)p.D, (uint64_t)p.T, (uint64_t)p.B};
+    const uint64_t strides[2] = {(uint64_t)p.x_st * 2, (uint64_t)(p.B > 1 ? p.x_sb : (int64_t)p.T * p.x_st) * 2};
+    const uint32_t box[3] = {(uint32_t)kSlice, (uint32_t)kWinTok, 1u};
+    if (make_tmap_bf16(&tmY, p.x, 3, dims, strides, box, false) != kOk) return -1;
+  }
+  tmY3 = tmY;
+  p.l3_bcast = 0;
+  if (l3v) {
+    p.l3_bcast = (p.l3_sb == 0 || p.B == 1) ? 1 : 0;
+    const uint64_t dims[3] = {(uint64_t)p.D, (uint64_t)p.T3, (uint64_t)(p.l3_bcast ? 1 : p.B)};
+    const uint64_t strides[2] = {(uint64_t)p.l3_st * 2,
+                                 (uint64_t)(p.l3_bcast ? (int64_t)p.T3 * p.l3_st : p.l3_sb) * 2};
+    const uint32_t box[3] = {(uint32_t)kSlice, (uint32_t)kWinTok, 1u};
+    if (make_tmap_bf16(&tmY3, p.l3, 3, dims, strides, box, false) != kOk) return -1;
+  }
+  tmCos = tmSin = tmY;
+  p.rope_bcast = 0;
+  if (rope) {
+    p.rope_bcast = (p.rope_sb == 0 || p.B == 1) ? 1 : 0;
+    const uint64_t dims[3] = {128u, (uint64_t)p.T, (uint64_t)(p.rope_bcast ? 1 : p.B)};
+    const uint64_t strides[2] = {(uint64_t)p.rope_st * 4,
+                                 (uint64_t)(p.rope_bcast ? (int64_t)p.T * p.rope_st : p.rope_sb) * 4};
+    const uint32_t box[3] = {128u, (uint32_t)kWinTok, 1u};
+    if (make_tmap_f32(&tmCos, p.rope_cos, 3, dims, strides, box) != kOk) return -1;
+    if (make_tmap_f32(&tmSin, p.rope_sin, 3, dims, strides, box) != kOk) return -1;
+  }
+  // Segments: one CTA per SM over all (batch row, slice, segment) triples.
+  // Slices with K heads (RoPE) cost more per token than V-only slices, so the
+  // two groups get their own segment lengths, split to even out CTA times:
+  // a V token costs about kv_cost of a K token.
+  const int sms = num_sms_current_device();
+  const int nds_k = (p.D / 2 + kSlice - 1) / kSlice;
+  const int nds_v = p.nds - nds_k;
+  const double kv_cost = rope ? win_v_cost() : 1.0;
+  auto seg_for = [&](int nseg) {
+    int len = (p.T + nseg - 1) / nseg;
+    return (len + kWinTok - 1) / kWinTok * kWinTok;
+  };
+  int best_k = 1, best_v = 1;
+  double best = 1e300;
+  for (int nk_seg = 1; nk_seg <= sms; ++nk_seg) {
+    const int64_t used = (int64_t)p.B * nds_k * nk_seg;
+    if (used > sms && nk_seg > 1) break;
+    int nv_seg = 1;
+    if (nds_v > 0) {
+      const int64_t left = sms - used;
+      if (left < (int64_t)p.B * nds_v && nk_seg > 1) break;  // the V slices would not fit in one wave
+      nv_seg = left / ((int64_t)p.B * nds_v) > 1 ? (int)(left / ((int64_t)p.B * nds_v)) : 1;
+    }
+    const double tk = seg_for(nk_seg) + W;
+    const double tv = nds_v > 0 ? (seg_for(nv_seg) + W) * kv_cost : 0.0;
+    const double tmax = tk > tv ? tk : tv;
+    if (tmax < best - 1e-9) {
+      best = tmax;
+      best_k = nk_seg;
+      best_v = nv_seg;
+    }
+  }
+  p.seg_len_k = seg_for(best_k);
+  p.seg_len_v = seg_for(best_v);
+  const int nseg_k = (p.T + p.seg_len_k - 1) / p.seg_len_k;
+  const int nseg_v = (p.T + p.seg_len_v - 1) / p.seg_len_v;
+  p.nds_k = nds_k;
+  p.n_ctas_k = p.B * nds_k * nseg_k;
+  const int64_t grid = (int64_t)p.n_ctas_k + (int64_t)p.B * nds_v * nseg_v;
+  if (grid > 0x7FFFFFFF) return -1;
+  p.win_tokens = W;
+  p.beta4 = (float)__builtin_powi((double)p.beta, 4);
+  p.beta32 = (float)__builtin_powi((double)p.beta, kWinTok);
+  const int g = (int)grid;
+  if (rope)
+    return bias ? (l3v ? launch_kv_window_t<true, true, true>(tmY, tmY3, tmCos, tmSin, p, g, stream)
+                       : launch_kv_window_t<true, true, false>(tmY, tmY3, tmCos, tmSin, p, g, stream))
+                : (l3v ? launch_kv_window_t<true, false, true>(tmY, tmY3, tmCos, tmSin, p, g, stream)
+                       : launch_kv_window_t<true, false, false>(tmY, tmY3, tmCos, tmSin, p, g, stream));
+  return bias ? (l3v ? launch_kv_window_t<false, true, true>(tmY, tmY3, tmCos, tmSin, p, g, stream)
+                     : launch_kv_window_t<false, true, false>(tmY, tmY3, tmCos, tmSin, p, g, stream))
+              : (l3v ? launch_kv_window_t<false, false, true>(tmY, tmY3, tmCos, tmSin, p, g, stream)
+                     : launch_kv_window_t<false, false, false>(tmY, tmY3, tmCos, tmSin, p, g, stream));
 }
 
 size_t route_ema_blend_workspace_bytes(int B, int T, int D) {
@@ -896,6 +1432,12 @@ int launch_route_ema_blend(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, c
   p.agg = reinterpret_cast<float*>(ws + flag_bytes);
   p.inc = p.agg + nrec * kSlice;
   p.status = device_status_word();
+  if (kv != nullptr && l2 == nullptr && ema_init == nullptr && ema_final == nullptr && logits != nullptr &&
+      !scan_general_forced()) {
+    // the layer's case: the streaming kernel (no flags, no look-back) when the tensors suit TMA
+    const int rc = launch_kv_window(p, stream);
+    if (rc >= 0) return rc;
+  }
   if (clear_flags && l2 == nullptr) {
     int rc = check_cuda(cudaMemsetAsync(ws, 0, flag_bytes, stream), "route_ema_blend memset");
     if (rc) return rc;
