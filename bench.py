@@ -619,6 +619,21 @@ def run_kernel_only(args):
     if args.only == "attn_prefill":
         flops = 4.0 * B * c["H"] * 128 * T * (T + 1) / 2
         line.update(batch=B, seq=T, tflops=round(flops / (ms * 1e-3) / 1e12, 1))
+        # the reference's default prefill path is torch SDPA (mka/layers/fastmka.py:134,157): the same
+        # q/k/v through torch.nn.functional.scaled_dot_product_attention (causal, GQA), timed the same way
+        sdpa = lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True,  # noqa: E731
+                                                                         enable_gqa=True)
+        for _ in range(args.warmup):
+            sdpa()
+        torch.cuda.synchronize()
+        torch.cuda._sleep(int(2e8))
+        e0.record()
+        for _ in range(args.steps):
+            sdpa()
+        e1.record()
+        torch.cuda.synchronize()
+        sms = e0.elapsed_time(e1) / max(args.steps, 1)
+        line.update(sdpa_ms=sms, sdpa_tflops=round(flops / (sms * 1e-3) / 1e12, 1))
     print(json.dumps(line))
 
 
