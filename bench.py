@@ -200,10 +200,16 @@ def _timed(dist, fn, steps):
 
 
 def _stage_times(fn, steps):
-    """Average duration (ms) of each forward stage over `steps` instrumented calls."""
+    """Average duration (ms) of each forward stage over `steps` instrumented calls.
+
+    A spin kernel queued ahead of each call (outside every measured interval)
+    lets the host enqueue the whole forward before the GPU reaches it, so the
+    stages run back to back and each event pair times the device, not a wait
+    for the host's next launch."""
     acc = {}
     for _ in range(steps):
         timers = []
+        torch.cuda._sleep(int(5e7))
         fn(timers)
         torch.cuda.synchronize()
         for name, s, e in timers:

@@ -19,7 +19,8 @@
 //               GEMMs run while the other tile's softmax runs
 //   warps 2,3   idle (complete the first warpgroup)
 //   warps 4..7  softmax of Q tile 0, warps 8..11 softmax of Q tile 1: thread =
-//               query row; reads its S row from TMEM, causal mask on diagonal
+//               query row; reads its S row from TMEM once into registers (216
+//               per thread through setmaxnreg), causal mask on diagonal
 //               tiles, running max m and sum z, writes P (bf16) back over S,
 //               rescales O in TMEM only when the max grew by more than 2^8
 //               (exact: the final 1/z uses the same stale max). One pair
@@ -41,15 +42,20 @@ constexpr int kBN = 128;        // keys per K/V tile
 constexpr int kHeadDim = 128;
 constexpr int kKS = 2;          // K/V ring stages
 constexpr int kThreads = 384;  // 3 warpgroups
-// Register split (setmaxnreg): the producer/MMA warpgroup gives registers to
-// the two softmax warpgroups. The launch holds kThreads x (registers ptxas
-// assigned); the split must fit in it or setmaxnreg.inc would wait forever, so
-// the launcher checks kMinLaunchRegs against the compiled kernel first.
+// Register split (setmaxnreg, issued at the top of each role's branch so that
+// ptxas allocates each role with its own budget): the producer/MMA warpgroup
+// gives registers to the two softmax warpgroups, which keep their whole S row
+// (128 scores) in registers from the max pass to the exponentials instead of
+// reading it from TMEM again (1.770 against 1.795 ms at batch 4 x 8192; 64/216
+// is the smallest control share ptxas compiles without spills). The launch
+// holds kThreads x (registers ptxas assigned); the split must fit in it or
+// setmaxnreg.inc would wait forever, so the launcher checks kMinLaunchRegs
+// against the compiled kernel first.
 #ifndef FMKA_ATTN_REG_SPLIT
-#define FMKA_ATTN_REG_SPLIT 0
+#define FMKA_ATTN_REG_SPLIT 1
 #endif
-constexpr int kRegsControl = 40;
-constexpr int kRegsSoftmax = 232;
+constexpr int kRegsControl = 64;
+constexpr int kRegsSoftmax = 216;
 constexpr int kMinLaunchRegs = (128 * kRegsControl + 256 * kRegsSoftmax + kThreads - 1) / kThreads;
 constexpr int kTileBytes = 128 * 128 * 2;   // 32 KB
 constexpr int kHalfBytes = kTileBytes / 2;  // one 64-column swizzle box
@@ -199,12 +205,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-#if FMKA_ATTN_REG_SPLIT
-  if (warp < 4) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
-  else asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
-#endif
 
   if (warp == 0) {
+#if FMKA_ATTN_REG_SPLIT
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
+#endif
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
       const int nt[2] = {n0, n1};
@@ -264,6 +269,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = last_v; j >= 0 && j > last_v - kKS; --j) mbar_wait(&v_full[j % kKS], (j / kKS) & 1, p.status);
     }
   } else if (warp == 1) {
+#if FMKA_ATTN_REG_SPLIT
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
+#endif
     // ----------------------------------------------------------------- MMA --
     if (lane == 0) {
       constexpr uint32_t id_s = make_idesc_bf16(kBM, kBN, false, false);
@@ -328,6 +336,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(mma_done, 0, p.status);
     }
   } else if (warp >= 4) {
+#if FMKA_ATTN_REG_SPLIT
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
+#endif
     // ------------------------------------------------------------- softmax --
     const int ti = (warp - 4) / 4;  // Q tile of this warpgroup
     const int quarter = warp & 3;   // TMEM lane quarter this warp may access
@@ -349,10 +360,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int kbase = j * kBN;
       const bool diag = kbase + kBN - 1 > qlim;  // this tile needs the causal / length mask
-      // ---- pass 1: row max over the 128 scores ----
+      // ---- pass 1: row max over the 128 scores (kept in registers for pass 2) ----
       float mx0;
+      uint32_t s[128];
       {
-        uint32_t s[128];
         tmem_ld32(lane_addr + s_col + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
         tmem_ld32(lane_addr + s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
         tmem_ld32(lane_addr + s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
@@ -410,18 +421,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
       for (int ch = 0; ch < 4; ++ch) {
-        uint32_t s[32];
-        tmem_ld32(lane_addr + s_col + 32 * ch, s);
-        tmem_wait_ld();
-        if (diag) {
-#pragma unroll
-          for (int c = 0; c < 32; ++c)
-            if (kbase + 32 * ch + c > qlim) s[c] = 0xFF800000u;
-        }
+        const uint32_t* sc = s + 32 * ch;  // masked in pass 1
         uint32_t pk[16];
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
-          const float2 xx = ffma2(make_float2(__uint_as_float(s[2 * c]), __uint_as_float(s[2 * c + 1])), sl2, nm2);
+          const float2 xx = ffma2(make_float2(__uint_as_float(sc[2 * c]), __uint_as_float(sc[2 * c + 1])), sl2, nm2);
           float2 pp;
           if ((c % FMKA_POLY_EVERY) == FMKA_POLY_EVERY - 1) {
             pp = exp2_poly2(xx);
@@ -496,6 +500,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+#if FMKA_ATTN_REG_SPLIT
+  else {  // warps 2 and 3 complete the first warpgroup's release
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
+  }
+#endif
 
   __syncwarp();
   tc_fence_before();
