@@ -798,6 +798,8 @@ constexpr int kWinRowBytes = kSlice * 2;                 // one token's 256 chan
 constexpr int kWinYBytes = kWinTok * kWinRowBytes;       // 16 KB
 constexpr int kWinRopeBytes = kWinTok * 128 * 4;         // 16 KB for cos, 16 KB for sin
 constexpr int kWinGateBytes = kWinTok * 16;             // float4 gate per token
+static_assert(kWinTpw == 4, "kv_window_kernel's powers beta^1..beta^4 assume 4 tokens per consumer warp");
+static_assert(kWinTok == 32, "the producer's lanes compute one gate each");
 constexpr int kWinSmemBudget = 200 * 1024;
 #ifndef FMKA_WIN_WARM_MULTI
 #define FMKA_WIN_WARM_MULTI 1
