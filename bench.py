@@ -447,6 +447,8 @@ def bench_long_context(args, dist, rank, world, device, peaks):
     achieved = flops / (attn_ms * 1e-3) / 1e12
     gsz = len(sh.plan.group)
     sh.close()
+    del q, k, v
+    recall = _l3_recall_line(x, steps, peaks, device, g)
     exchange = ("none" if gsz == 1 else "peer stores from the attention and o_proj epilogues"
                 if args.exchange == "peer" else "NCCL all-gather, o_proj on every rank")
     return {"metric": "FastMKA prefill tokens/s, long context with L3 (fixed total work)",
@@ -454,11 +456,41 @@ def bench_long_context(args, dist, rank, world, device, peaks):
             "config": {"batch": B, "seq_len": T, "d_model": D, "heads": f"{c['H']}/{c['HKV']}", "levels": 3,
                        "router": f"{D}->{c['R']}->3", "partition": f"sequences x kv heads, group size "
                                                                   f"{gsz}", "exchange": exchange},
-            "exchange_kernel": xk,
+            "exchange_kernel": xk, "l3_recall": recall,
             "roofline": {"bound": "tensor", "kernel": "attn_prefill (this rank's heads, T=32768)",
                          "achieved": round(achieved, 1), "peak": peaks["bf16"], "unit": "TFLOP/s",
                          "frac": round(achieved / peaks["bf16"], 4), "peak_kind": f"{peaks['src']} burst bf16",
                          "launch_ms": attn_ms}}
+
+
+def _l3_recall_line(x, steps, peaks, device, g, n_chunks=8192, top_r=8, block_len=64):
+    """The L3 chunk recall that produces R (mka_b200.l3) for this rank's sequences:
+    a bank of n_chunks seeded N(0, 0.5) chunk keys and values (standing in for the
+    chunk means of an earlier 512k-token context), the top-8 chunks of every
+    64-token block. Timed on its own: the layer step above takes its R as given,
+    as the reference's layers do."""
+    from mka_b200.l3 import L3ChunkStore
+
+    Bl, T, D = x.shape
+    keys = (torch.randn(n_chunks, D, generator=g, device=device) * 0.5).to(torch.bfloat16)
+    vals = (torch.randn(n_chunks, D, generator=g, device=device) * 0.5).to(torch.bfloat16)
+    store = L3ChunkStore(keys, vals)
+    for _ in range(2):
+        store.recall(x, top_r, block_len)
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(2e8))
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        store.recall(x, top_r, block_len)
+    e.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(e) / steps
+    hbm = 2 * Bl * T * D * 2  # x read for the block means + R written
+    return {"ms": ms, "bank_chunks": n_chunks, "top_r": top_r, "block_len": block_len, "rows": Bl * T,
+            "hbm_bytes": hbm, "achieved_gbs": round(hbm / (ms * 1e-3) / 1e9, 1),
+            "frac_of_hbm": round(hbm / (ms * 1e-3) / 1e9 / peaks["hbm"], 4),
+            "kernels": "block means, scores GEMM (fp32 out), top-R, weighted gather"}
 
 
 # -------------------------------------------------------------- CPU (oracle) --

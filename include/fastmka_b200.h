@@ -46,6 +46,10 @@
  *   fmka_silu_mul_bf16      SiLU product of the decoder layers around the patched
  *                           self_attn (transformers LlamaRMSNorm / LlamaMLP), one
  *                           pass each
+ *   fmka_l3_*, fmka_gemm_bf16_f32out
+ *                           the L3 chunk recall producing R, which the reference
+ *                           describes (memory_hierarchy.py:1-10,30-34) but does
+ *                           not implement
  *   fmka_attn_fwd_prefill_scatter, fmka_gemm_bf16_kblocked_scatter, fmka_peer_*
  *                           the head-sharded layer over several GPUs of a box:
  *                           attention rows and o_proj rows stored straight into
@@ -108,6 +112,12 @@ FMKA_API int fmka_num_sms(void);
  * fp32 accumulation (tcgen05). K, lda, ldw, ldc multiples of 8. */
 FMKA_API int fmka_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, const float* bias, void* c, int64_t ldc,
                    int M, int N, int K, fmka_stream_t stream);
+
+/* fmka_gemm_bf16_f32out: C[M, N] = A[M, K] * W[N, K]^T with bf16 operands and an
+ * fp32 output (row stride ldc, a multiple of 8; C 16-byte aligned). Scores of
+ * the L3 chunk recall (no counterpart in the reference). */
+FMKA_API int fmka_gemm_bf16_f32out(const void* a, int64_t lda, const void* w, int64_t ldw, float* c, int64_t ldc,
+                                   int M, int N, int K, fmka_stream_t stream);
 
 /* fmka_gemm_bf16_kblocked: the same GEMM with A stored as K / a_kblk blocks of
  * [M, a_kblk] (row stride lda, blocks a_blk_stride elements apart): A[m, k] =
@@ -266,6 +276,30 @@ FMKA_API int fmka_rmsnorm_bf16(const void* x, int64_t ldx, const void* w, float 
  * out[i] = bf16(bf16(silu(g[i])) * u[i]) for n contiguous bf16 elements (n a
  * multiple of 8); out may be g. */
 FMKA_API int fmka_silu_mul_bf16(const void* g, const void* u, void* out, int64_t n, fmka_stream_t stream);
+
+/* ------------------------------------------------------ L3 chunk recall ---
+ * The retrieval that produces the L3 memory R from a bank of historical chunks.
+ * The reference describes it (mka/config/memory_hierarchy.py:1-10,30-34:
+ * "DRAM (vectorized hash, chunk recall)", l3_recall_top_r "top-R chunks per
+ * query") and implements none; this algorithm is the library's own:
+ *   q = fmka_l3_block_mean_bf16(x)             block summaries, bf16 [B*nq, D],
+ *                                              nq = ceil(T / block_len)
+ *   s = fmka_gemm_bf16_f32out(q, keys)         fp32 scores [B*nq, n_chunks]
+ *   (idx, w) = fmka_l3_topr_f32(s, R, scale)   the R best chunks of each row
+ *                                              (ties: lower index first) and
+ *                                              softmax(scale * score) over them
+ *   R = fmka_l3_recall_gather_bf16(idx, w, values)
+ *                                              R[b, t] = sum_r w values[idx] for
+ *                                              every token t of block t / block_len
+ * x, values, out: bf16 with contiguous channels, strides in elements, multiples
+ * of 8; D a multiple of 8; R in 1..32 and at most n_chunks. */
+FMKA_API int fmka_l3_block_mean_bf16(const void* x, int64_t x_sb, int64_t x_st, int B, int T, int D, int block_len,
+                                     void* q, int64_t ldq, fmka_stream_t stream);
+FMKA_API int fmka_l3_topr_f32(const float* scores, int64_t lds, int M, int N, int R, float scale, int32_t* idx,
+                              float* w, fmka_stream_t stream);
+FMKA_API int fmka_l3_recall_gather_bf16(const int32_t* idx, const float* w, int R, const void* values, int64_t ldv,
+                                        int n_chunks, int D, int B, int T, int block_len, void* out, int64_t o_sb,
+                                        int64_t o_st, fmka_stream_t stream);
 
 /* ------------------------------------------------ several GPUs of a box ---
  * The ranks of a sequence group (one process per GPU) share buffers through

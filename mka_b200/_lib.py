@@ -56,6 +56,10 @@ _SIGNATURES = {
     "fmka_peer_barrier": (_I, [_P, _I, _I, c_uint32, _P]),
     "fmka_rmsnorm_bf16": (_I, [_P, _L, _P, _F, _P, _L, _I, _I, _P]),
     "fmka_silu_mul_bf16": (_I, [_P, _P, _P, _L, _P]),
+    "fmka_gemm_bf16_f32out": (_I, [_P, _L, _P, _L, _P, _L, _I, _I, _I, _P]),
+    "fmka_l3_block_mean_bf16": (_I, [_P, _L, _L, _I, _I, _I, _I, _P, _L, _P]),
+    "fmka_l3_topr_f32": (_I, [_P, _L, _I, _I, _I, _F, _P, _P, _P]),
+    "fmka_l3_recall_gather_bf16": (_I, [_P, _P, _I, _P, _L, _I, _I, _I, _I, _I, _P, _L, _L, _P]),
     "fmka_attn_decode_num_splits": (_I, [_I, _I, _I]),
     "fmka_attn_decode_workspace_size": (c_size_t, [_I, _I, _I, _I, _I]),
     "fmka_attn_decode_splitkv": (_I, [_P, _L, _L, _P, _P, _L, _L, _L, _P, _L, _L, _P, _L,

@@ -19,7 +19,7 @@ INCLUDE = PKG_DIR.parent / "include"
 LIB_NAME = "libfastmka_b200.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-SOURCES = ["capi.cu", "gemm.cu", "route_scan.cu", "attn_prefill.cu", "attn_decode.cu", "peer.cu", "norm.cu"]
+SOURCES = ["capi.cu", "gemm.cu", "route_scan.cu", "attn_prefill.cu", "attn_decode.cu", "peer.cu", "norm.cu", "l3_recall.cu"]
 HEADERS = ["ptx.cuh", "fmka_internal.h"]
 
 NVCC_FLAGS = [

@@ -47,6 +47,13 @@ int launch_rmsnorm(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* w, 
                    int64_t ldy, int rows, int D, cudaStream_t stream);
 int launch_silu_mul(const __nv_bfloat16* g, const __nv_bfloat16* u, __nv_bfloat16* out, int64_t n,
                     cudaStream_t stream);
+int launch_block_mean(const __nv_bfloat16* x, int64_t x_sb, int64_t x_st, int B, int T, int D, int L,
+                      __nv_bfloat16* q, int64_t ldq, cudaStream_t stream);
+int launch_topr(const float* scores, int64_t lds, int M, int N, int R, float scale, int* idx, float* w,
+                cudaStream_t stream);
+int launch_recall_gather(const int* idx, const float* w, int R, const __nv_bfloat16* values, int64_t ldv, int nv,
+                         int D, int B, int T, int L, __nv_bfloat16* out, int64_t o_sb, int64_t o_st,
+                         cudaStream_t stream);
 size_t attn_decode_workspace_bytes(int B, int Hq, int num_splits);
 int attn_decode_plan(int B, int Hkv, int Tk, int requested, int* keys_per_split_out);
 int launch_attn_decode(const __nv_bfloat16* q, int64_t q_sb, int64_t q_sh, const __nv_bfloat16* k,
@@ -232,6 +239,26 @@ int fmka_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, const
   p.seg[0].out = bfw(c);
   p.seg[0].ld = ldc;
   p.seg[0].bias = bias;
+  p.seg[1] = empty_seg();
+  p.status = device_status_word();
+  return launch_gemm(bf(a), lda, bf(w), ldw, p, num_sms_current_device(), as_stream(stream));
+}
+
+int fmka_gemm_bf16_f32out(const void* a, int64_t lda, const void* w, int64_t ldw, float* c, int64_t ldc, int M,
+                          int N, int K, fmka_stream_t stream) {
+  if (a == nullptr || w == nullptr || c == nullptr) return set_error(kErrInvalidArgument, "gemm: null pointer");
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.n_split = N;
+  p.seg[0] = empty_seg();
+  p.seg[0].kind = kSegRowMajorF32;
+  p.seg[0].n_begin = 0;
+  p.seg[0].n_end = N;
+  p.seg[0].out_f32 = c;
+  p.seg[0].ld = ldc;
   p.seg[1] = empty_seg();
   p.status = device_status_word();
   return launch_gemm(bf(a), lda, bf(w), ldw, p, num_sms_current_device(), as_stream(stream));
@@ -472,6 +499,28 @@ int fmka_rmsnorm_bf16(const void* x, int64_t ldx, const void* w, float eps, void
 int fmka_silu_mul_bf16(const void* g, const void* u, void* out, int64_t n, fmka_stream_t stream) {
   if (g == nullptr || u == nullptr || out == nullptr) return set_error(kErrInvalidArgument, "silu_mul: null pointer");
   return launch_silu_mul(bf(g), bf(u), bfw(out), n, as_stream(stream));
+}
+
+int fmka_l3_block_mean_bf16(const void* x, int64_t x_sb, int64_t x_st, int B, int T, int D, int block_len,
+                            void* q, int64_t ldq, fmka_stream_t stream) {
+  if (x == nullptr || q == nullptr) return set_error(kErrInvalidArgument, "block_mean: null pointer");
+  return launch_block_mean(bf(x), x_sb, x_st, B, T, D, block_len, bfw(q), ldq, as_stream(stream));
+}
+
+int fmka_l3_topr_f32(const float* scores, int64_t lds, int M, int N, int R, float scale, int32_t* idx, float* w,
+                     fmka_stream_t stream) {
+  if (scores == nullptr || idx == nullptr || w == nullptr) return set_error(kErrInvalidArgument, "topr: null pointer");
+  if (!std::isfinite(scale)) return set_error(kErrInvalidArgument, "topr: scale must be finite");
+  return launch_topr(scores, lds, M, N, R, scale, idx, w, as_stream(stream));
+}
+
+int fmka_l3_recall_gather_bf16(const int32_t* idx, const float* w, int R, const void* values, int64_t ldv, int n_chunks,
+                               int D, int B, int T, int block_len, void* out, int64_t o_sb, int64_t o_st,
+                               fmka_stream_t stream) {
+  if (idx == nullptr || w == nullptr || values == nullptr || out == nullptr)
+    return set_error(kErrInvalidArgument, "recall_gather: null pointer");
+  return launch_recall_gather(idx, w, R, bf(values), ldv, n_chunks, D, B, T, block_len, bfw(out), o_sb, o_st,
+                              as_stream(stream));
 }
 
 int fmka_attn_fwd_prefill_scatter(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, const void* k,

@@ -47,7 +47,7 @@ struct PeerPtrs {
 };
 
 // ------------------------------------------------------------------- GEMM --
-enum SegKind : int { kSegRowMajor = 0, kSegHeads = 1, kSegRouter = 2, kSegSwiGLU = 3 };
+enum SegKind : int { kSegRowMajor = 0, kSegHeads = 1, kSegRouter = 2, kSegSwiGLU = 3, kSegRowMajorF32 = 4 };
 
 struct GemmSeg {
   int kind;
@@ -67,6 +67,7 @@ struct GemmSeg {
   int L;
   int act;               // 0 = SiLU, 1 = GELU (erf)
   float* logits;         // [M, L] fp32, accumulated
+  float* out_f32;        // kSegRowMajorF32: [M, ld] fp32 output (row stride ld)
   // SwiGLU: columns come in blocks of 256, gate rows then up rows of the same
   // 128 output channels; out [M, ld] receives silu(gate) * up per channel.
 };

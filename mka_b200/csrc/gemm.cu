@@ -70,6 +70,21 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const uint32_t (
   }
 }
 
+// 32 fp32 values of one row (the first nvalid of them).
+__device__ __forceinline__ void store_row32_f32(float* dst, const uint32_t (&r)[32], int nvalid) {
+  if (nvalid >= 32 && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
+    float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      d4[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
+                          __uint_as_float(r[4 * q + 3]));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < nvalid) dst[j] = __uint_as_float(r[j]);
+  }
+}
+
 // Fused epilogue of one accumulator tile for the calling thread's row `m` (a
 // warp's lanes hold 32 consecutive rows): columns n0 .. n0+BN-1 of the output
 // from TMEM at acc_addr (this warp's lane quarter, the tile's first column).
@@ -78,7 +93,16 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams& p, int m, b
                                                    uint32_t acc_addr) {
   const GemmSeg& sg = (n0 >= p.n_split) ? p.seg[1] : p.seg[0];
 
-  if (sg.kind == kSegRowMajor) {
+  if (sg.kind == kSegRowMajorF32) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(acc_addr + c * 32, r);
+      tmem_wait_ld();
+      const int n = n0 + c * 32;
+      if (row_ok && n < sg.n_end) store_row32_f32(sg.out_f32 + (int64_t)m * sg.ld + (n - sg.n_begin), r, sg.n_end - n);
+    }
+  } else if (sg.kind == kSegRowMajor) {
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       uint32_t r[32];
@@ -988,10 +1012,12 @@ int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int
       return set_error(kErrUnsupported, "gemm: head-split epilogue needs head_dim 128 and whole heads");
     if (g.kind == kSegRouter && (g.L < 1 || g.L > 4 || g.w2 == nullptr || g.logits == nullptr))
       return set_error(kErrInvalidArgument, "gemm: router epilogue needs 1..4 levels, w2 and logits");
-    if (g.kind == kSegRowMajor && (g.ld % 8 != 0))
+    if ((g.kind == kSegRowMajor || g.kind == kSegRowMajorF32) && (g.ld % 8 != 0))
       return set_error(kErrInvalidArgument, "gemm: output row stride must be a multiple of 8");
+    if (g.kind == kSegRowMajorF32 && (g.out_f32 == nullptr || (reinterpret_cast<uintptr_t>(g.out_f32) & 15u)))
+      return set_error(kErrInvalidArgument, "gemm: the fp32 output must be 16-byte aligned");
     // an output row must not run into the next one
-    if (p.n_dst == 0 && g.kind == kSegRowMajor && g.ld < g.n_end - g.n_begin)
+    if (p.n_dst == 0 && (g.kind == kSegRowMajor || g.kind == kSegRowMajorF32) && g.ld < g.n_end - g.n_begin)
       return set_error(kErrInvalidArgument, "gemm: output row stride is smaller than the row");
     if (g.kind == kSegSwiGLU && g.ld < (g.n_end - g.n_begin) / 2)
       return set_error(kErrInvalidArgument, "gemm: output row stride is smaller than the row");

@@ -488,6 +488,88 @@ def silu_mul(g: torch.Tensor, u: torch.Tensor, out: Optional[torch.Tensor] = Non
     return out
 
 
+# ------------------------------------------------------------ L3 recall --
+def gemm_f32out(a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[M, N] = a[M, K] @ w[N, K]^T in fp32 (bf16 operands, tcgen05)."""
+    _check_cuda(a, w)
+    _check_bf16(a, w)
+    if a.dim() != 2 or w.dim() != 2 or a.shape[1] != w.shape[1]:
+        raise RuntimeError("gemm_f32out: expected a [M, K] and w [N, K]")
+    if a.stride(1) != 1 or w.stride(1) != 1:
+        raise RuntimeError("gemm_f32out: inner dimension must be contiguous")
+    M, K = a.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, (N + 7) // 8 * 8), dtype=torch.float32, device=a.device)[:, :N]
+    _lib.call("fmka_gemm_bf16_f32out", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(),
+              out.stride(0), M, N, K, _stream(a))
+    return out
+
+
+def l3_block_mean(x: torch.Tensor, block_len: int) -> torch.Tensor:
+    """Block summaries q[b * nq + j] = bf16(mean of x[b, j*L:(j+1)*L]) of x [B, T, D]
+    (nq = ceil(T / L), the last block partial): the queries of the L3 recall."""
+    _check_cuda(x)
+    _check_bf16(x)
+    if x.dim() != 3 or x.stride(2) != 1:
+        raise RuntimeError("l3_block_mean: x must be [B, T, D] with contiguous channels")
+    B, T, D = x.shape
+    nq = (T + block_len - 1) // block_len
+    q = torch.empty((B * nq, D), dtype=torch.bfloat16, device=x.device)
+    _lib.call("fmka_l3_block_mean_bf16", x.data_ptr(), x.stride(0), x.stride(1), B, T, D, block_len,
+              q.data_ptr(), q.stride(0), _stream(x))
+    return q
+
+
+def l3_topr(scores: torch.Tensor, top_r: int, scale: float) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The top_r best columns of every row of scores [M, N] (fp32; ties: the lower
+    index first) and softmax(scale * score) over them: idx int32 [M, R], w fp32 [M, R]."""
+    _check_cuda(scores)
+    if scores.dtype != torch.float32 or scores.dim() != 2 or scores.stride(1) != 1:
+        raise RuntimeError("l3_topr: scores must be fp32 [M, N] with contiguous rows")
+    M, N = scores.shape
+    idx = torch.empty((M, top_r), dtype=torch.int32, device=scores.device)
+    w = torch.empty((M, top_r), dtype=torch.float32, device=scores.device)
+    _lib.call("fmka_l3_topr_f32", scores.data_ptr(), scores.stride(0), M, N, top_r, float(scale),
+              idx.data_ptr(), w.data_ptr(), _stream(scores))
+    return idx, w
+
+
+def l3_recall_gather(idx: torch.Tensor, w: torch.Tensor, values: torch.Tensor, B: int, T: int, block_len: int,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """R[b, t] = sum_r w[b * nq + t // L, r] * values[idx[.., r]] for every token: [B, T, D] bf16."""
+    _check_cuda(idx, w, values)
+    _check_bf16(values)
+    if idx.dtype != torch.int32 or w.dtype != torch.float32 or idx.shape != w.shape or not idx.is_contiguous() \
+            or not w.is_contiguous():
+        raise RuntimeError("l3_recall_gather: idx int32 and w fp32 of the same contiguous shape [M, R]")
+    if values.dim() != 2 or values.stride(1) != 1:
+        raise RuntimeError("l3_recall_gather: values must be [n_chunks, D] with contiguous channels")
+    n_chunks, D = values.shape
+    if out is None:
+        out = torch.empty((B, T, D), dtype=torch.bfloat16, device=values.device)
+    _lib.call("fmka_l3_recall_gather_bf16", idx.data_ptr(), w.data_ptr(), idx.shape[1], values.data_ptr(),
+              values.stride(0), n_chunks, D, B, T, block_len, out.data_ptr(), out.stride(0), out.stride(1),
+              _stream(values))
+    return out
+
+
+def l3_chunk_recall(x: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, top_r: int, block_len: int = 64,
+                    scale: Optional[float] = None) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """The L3 memory R [B, T, D] recalled for x [B, T, D] from a chunk bank (keys,
+    values [n_chunks, D] bf16): block summaries of x score every key, each block
+    takes its top_r chunks and softmax(scale * score) weights (scale defaults to
+    1/sqrt(D)), and every token of the block receives their weighted sum.
+    Returns (R, idx [B * nq, top_r] int32, w [B * nq, top_r] fp32)."""
+    B, T, D = x.shape
+    if keys.shape != values.shape or keys.shape[1] != D:
+        raise RuntimeError("l3_chunk_recall: keys and values must both be [n_chunks, D]")
+    q = l3_block_mean(x, block_len)
+    scores = gemm_f32out(q, keys)
+    idx, w = l3_topr(scores, top_r, D ** -0.5 if scale is None else scale)
+    return l3_recall_gather(idx, w, values, B, T, block_len), idx, w
+
+
 # ---------------------------------------- reference-compatible op wrappers --
 def has_fastmka_cuda() -> bool:
     """True when the library loads and a CUDA device is visible (mka/cuda/ops.py:25-26)."""

@@ -233,3 +233,55 @@ def hf_fastmka_forward(h: Tensor, p: Dict[str, Tensor], num_heads: int, num_kv_h
     o = attention(qs, repeat_kv(ks, g), repeat_kv(vs, g), use_sdpa=past is None)
     out = F.linear(o.transpose(1, 2).contiguous().view(b, t, d), p["wo"], p.get("bo"))
     return {"out": out, "k": ks, "v": vs, "lam": lam, "lse": attention_lse(qs, ks) if with_lse else None}
+
+
+# ------------------------------------------------------------ L3 chunk recall --
+# The reference describes the L3 tier (mka/config/memory_hierarchy.py:1-10,
+# "DRAM (vectorized hash, chunk recall)"; lines 30-34, l3_recall_top_r "top-R
+# chunks per query") and implements no recall, so nothing here is pinned to the
+# reference: this restates the recall of mka_b200.l3 / l3_recall.cu (block-mean
+# queries, dot-product scores, top-R with the lower index first on ties,
+# softmax weights, one weighted sum per query block) so that the kernels can be
+# checked against it.
+def l3_block_mean(x: Tensor, block_len: int) -> Tensor:
+    """bf16-rounded means of block_len-token blocks of x [B, T, D] -> [B * nq, D] (fp32 values)."""
+    b, t, d = x.shape
+    nq = (t + block_len - 1) // block_len
+    out = torch.empty(b, nq, d, dtype=torch.float64)
+    xd = x.double()
+    for j in range(nq):
+        out[:, j] = xd[:, j * block_len:min((j + 1) * block_len, t)].mean(1)
+    return out.float().bfloat16().float().reshape(b * nq, d)
+
+
+def l3_topr(scores: Tensor, top_r: int, scale: float) -> Tuple[Tensor, Tensor]:
+    """Per row: the top_r best columns (score descending, the lower index first on
+    ties) and softmax(scale * score) over them."""
+    m, n = scores.shape
+    idx = torch.empty(m, top_r, dtype=torch.int64)
+    w = torch.empty(m, top_r, dtype=torch.float32)
+    cols = torch.arange(n)
+    for i in range(m):
+        s = scores[i].double()
+        order = sorted(range(n), key=lambda c: (-s[c].item(), c))[:top_r]
+        idx[i] = torch.tensor(order)
+        sel = s[cols[order]]
+        e = torch.exp((sel - sel.max()) * scale)
+        w[i] = (e / e.sum()).float()
+    return idx, w
+
+
+def l3_chunk_recall(x: Tensor, keys: Tensor, values: Tensor, top_r: int, block_len: int,
+                    scale: Optional[float] = None, q: Optional[Tensor] = None):
+    """R [B, T, D], idx, w and the scores for x [B, T, D] and a chunk bank keys /
+    values [n_chunks, D]; q (the block summaries) may be given, e.g. the GPU's
+    own, so that a ranking comparison does not hinge on a bf16 rounding."""
+    b, t, d = x.shape
+    q = l3_block_mean(x, block_len) if q is None else q.float()
+    scores = q.double() @ keys.double().t()
+    idx, w = l3_topr(scores, top_r, d ** -0.5 if scale is None else scale)
+    vecs = (w.double().unsqueeze(-1) * values.double()[idx]).sum(1)  # [B * nq, D]
+    nq = (t + block_len - 1) // block_len
+    rows = torch.arange(t) // block_len
+    r = vecs.view(b, nq, d)[:, rows]
+    return r.float(), idx, w, scores

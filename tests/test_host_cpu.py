@@ -74,6 +74,29 @@ def test_argument_errors_of_the_newer_entry_points():
     assert lib.fmka_peer_barrier(flags, 2, 2, 1, None) == 1  # rank outside the group
     assert lib.fmka_peer_barrier(flags, 0, 9, 1, None) == 1  # more than 8 ranks
     assert lib.fmka_peer_alloc(0, ctypes.byref(P())) == 1
+    # L3 chunk recall
+    rc = lib.fmka_l3_topr_f32(c, 64, 10, 64, 33, 1.0, a, w, None)  # R > 32
+    assert rc == 2 and "1..32" in _lib.last_error()[1]
+    rc = lib.fmka_l3_topr_f32(c, 64, 10, 4, 8, 1.0, a, w, None)  # R > N
+    assert rc == 1 and "exceeds" in _lib.last_error()[1]
+    rc = lib.fmka_l3_topr_f32(c, 32, 10, 64, 4, 1.0, a, w, None)  # row stride < N
+    assert rc == 1 and "row stride" in _lib.last_error()[1]
+    rc = lib.fmka_l3_block_mean_bf16(a, 0, 100, 1, 16, 100, 4, c, 100, None)  # D = 100 not a multiple of 8
+    assert rc == 1 and "multiples of 8" in _lib.last_error()[1]
+    rc = lib.fmka_l3_recall_gather_bf16(a, w, 0, c, 64, 10, 64, 1, 16, 4, c, 64, 64, None)  # R = 0
+    assert rc == 2 and "1..32" in _lib.last_error()[1]
+    rc = lib.fmka_gemm_bf16_f32out(a, 64, w, 64, None, 64, 128, 64, 64, None)
+    assert rc == 1 and "null" in _lib.last_error()[1]
+
+
+def test_l3_store_validates_its_bank():
+    """Host checks of the L3 chunk bank (no device work)."""
+    from mka_b200.l3 import L3ChunkStore
+
+    with pytest.raises(ValueError, match="bf16 CUDA"):
+        L3ChunkStore(torch.zeros(8, 64, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="n_chunks, D"):
+        L3ChunkStore(torch.zeros(8, 64), torch.zeros(8, 32))
 
 
 def test_workspace_sizes():

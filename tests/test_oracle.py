@@ -1,6 +1,8 @@
 """Pins the CPU oracle (oracle/fastmka_oracle.py) to the reference: every golden
 fixture was produced by running the FastLM/MKA modules themselves
 (tests/golden/make_golden.py); the oracle must reproduce them in fp32."""
+import math
+
 import pytest
 import torch
 
@@ -165,3 +167,30 @@ def test_oracle_fused_route_op_matches_reference_module(name):
     q = F.linear(x, p["wq"]).view(b, t, h, d // h).transpose(1, 2)
     o = orc.fused_route_mka_op(q, x, orc.causal_prefix_ema(x, float(c["beta"])), l3, c["lam"], p["wk"], p["wv"])
     _close(F.linear(o.transpose(1, 2).reshape(b, t, d), p["wo"]), c["out"])
+
+
+def test_oracle_l3_recall_against_brute_force():
+    """The oracle's L3 recall (the package's own algorithm: the reference describes
+    the tier, mka/config/memory_hierarchy.py:1-10,30-34, and implements none)
+    against a direct restatement: block means, every score, a full sort with the
+    lower index first on ties, softmax weights, and the per-token weighted sum."""
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(2, 75, 16, generator=g)
+    keys = torch.randn(20, 16, generator=g)
+    keys[7] = keys[3]  # a tie: chunk 3 must rank before chunk 7
+    vals = torch.randn(20, 16, generator=g)
+    r, idx, w, s = orc.l3_chunk_recall(x, keys, vals, 4, 32, scale=0.5)
+    for b in range(2):
+        for j in range(3):
+            blk = x[b, j * 32:min(j * 32 + 32, 75)].double().mean(0).float().bfloat16().float()
+            sc = [float(blk.double() @ keys[c].double()) for c in range(20)]
+            order = sorted(range(20), key=lambda c: (-sc[c], c))[:4]
+            assert idx[b * 3 + j].tolist() == order
+            if 3 in order and 7 in order:
+                assert order.index(3) < order.index(7)
+            e = torch.tensor([math.exp(0.5 * (sc[c] - sc[order[0]])) for c in order])
+            wt = e / e.sum()
+            assert torch.allclose(w[b * 3 + j], wt.float(), atol=1e-6)
+            vec = sum(wt[i].item() * vals[order[i]].double() for i in range(4))
+            for t in range(j * 32, min(j * 32 + 32, 75)):
+                assert torch.allclose(r[b, t].double(), vec, atol=1e-5)
