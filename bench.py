@@ -632,6 +632,19 @@ def run_kernel_only(args):
             fn = lambda: ops.gemm_kblocked_scatter(a, w, None, ptrs, 0, cl["D"])  # noqa: E731
         else:
             fn = lambda: ops.gemm_kblocked(a, w)  # noqa: E731
+    elif args.only == "l3_recall":
+        # the L3 chunk recall at the long-context size (per batch row --batch, default 2):
+        # a bank of 8192 seeded chunks, the top-8 chunks of every 64-token block
+        from mka_b200.l3 import L3ChunkStore
+
+        cl = LONG
+        B = args.batch or cl["B"]
+        T = args.seq or cl["T"]
+        x = torch.randn(B, T, cl["D"], generator=g, device=dev).mul_(0.5).to(torch.bfloat16)
+        keys = torch.randn(8192, cl["D"], generator=g, device=dev).mul_(0.5).to(torch.bfloat16)
+        vals = torch.randn(8192, cl["D"], generator=g, device=dev).mul_(0.5).to(torch.bfloat16)
+        store = L3ChunkStore(keys, vals)
+        fn = lambda: store.recall(x, top_r=8, block_len=64)  # noqa: E731
     elif args.only == "attn_decode":
         B = args.batch or d["B"]
         q = torch.randn(B, d["H"], 1, 128, generator=g, device=dev, dtype=torch.bfloat16)
@@ -861,7 +874,7 @@ def main():
                     help="skip the full Llama-3-8B model measurement (one GPU only)")
     ap.add_argument("--only", default=None,
                     help="run one kernel alone (attn_prefill, attn_decode, route_ema_blend, route_ema_blend_h, "
-                         "qr_proj, kv_gemm, kv_proj, o_proj, o_proj_scatter, o_proj_blocked)")
+                         "qr_proj, kv_gemm, kv_proj, o_proj, o_proj_scatter, o_proj_blocked, l3_recall)")
     ap.add_argument("--batch", type=int, default=0, help="batch override for --only")
     ap.add_argument("--seq", type=int, default=0, help="sequence-length override for --only (prefill kernels)")
     args = ap.parse_args()
