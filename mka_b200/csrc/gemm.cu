@@ -769,14 +769,24 @@ constexpr int kSplitRows = 64;   // rows of a partial that are exchanged
 // CTA's pipeline-fill latency and the two cluster barriers outweigh the
 // extra streaming CTAs, and clusters of 7 pack poorly into the GPCs).
 constexpr int kSplitMax = 2;
+// Cluster size with 64-column tiles (row-major outputs). Measured on the
+// decode step (M = 64, K = 4096): 64-column tiles in pairs took kv_proj
+// (N = 2048) and o_proj (N = 4096) from 0.0229 to 0.0208 ms each; clusters of
+// 4 took kv_proj to 0.0189 ms and did not show in the step's time.
+#ifndef FMKA_SPLITK_MAX64
+#define FMKA_SPLITK_MAX64 2
+#endif
+constexpr int kSplitMax64 = FMKA_SPLITK_MAX64;
+constexpr int split_max_for(int bn) { return bn == 64 ? kSplitMax64 : kSplitMax; }
 
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ GemmParams p) {
-  constexpr int BN = 128;
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
-  constexpr int kSlotBytes = kSplitRows * BN * 4;  // 32 KB
+  constexpr int kSlotBytes = kSplitRows * BN * 4;  // 32 KB at BN = 128
+  static_assert((split_max_for(BN) - 1) * kSlotBytes <= S * Cfg::kStageBytes, "the partials fit the stage buffers");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -795,7 +805,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t rank = cluster_ctarank();
   uint32_t csize;
   asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(csize));
-  const int tile = blockIdx.x / (int)csize;  // 128-column tile of this cluster
+  const int tile = blockIdx.x / (int)csize;  // BN-column tile of this cluster
   const int n0 = tile * BN;
   const int num_kb = (p.K + kBK - 1) / kBK;
   // balanced slices: none is empty while the cluster has at most num_kb CTAs
@@ -1062,17 +1072,45 @@ int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int
     const char* e = std::getenv("FMKA_GEMM_SPLITK");
     return e == nullptr || e[0] != '0';
   }();
+  // Row-major outputs only (no head-split, router or SwiGLU epilogue, which need
+  // whole 128-column heads or blocks): 64-column tiles, twice the CTAs streaming
+  // the weights (the MMA's N = 64 runs at half rate, which a weight-bound GEMM
+  // does not feel). FMKA_GEMM_SPLIT64=0 keeps 128-column tiles.
+  static const bool split64_enabled = [] {
+    const char* e = std::getenv("FMKA_GEMM_SPLIT64");
+    return e == nullptr || e[0] != '0';
+  }();
+  auto row_major_only = [&]() {
+    for (int sg = 0; sg < 2; ++sg) {
+      const GemmSeg& g = p.seg[sg];
+      if (g.n_end > g.n_begin && g.kind != kSegRowMajor && g.kind != kSegRowMajorF32) return false;
+    }
+    return true;
+  };
   if (!scatter && splitk_enabled && BN == 128 && p.M <= kSplitRows) {
-    const int tiles = (p.N + BN - 1) / BN;
     const int num_kb = (p.K + kBK - 1) / kBK;
-    int cs = num_sms / tiles;
-    if (cs > kSplitMax) cs = kSplitMax;
-    if (cs > num_kb) cs = num_kb;
+    auto cluster_for = [&](int bn) {
+      int c = num_sms / ((p.N + bn - 1) / bn);
+      if (c > split_max_for(bn)) c = split_max_for(bn);
+      if (c > num_kb) c = num_kb;
+      return c;
+    };
+    // 64-column tiles only where they still leave two CTAs per tile
+    const int bn = (split64_enabled && row_major_only() && p.n_split >= p.N && cluster_for(64) >= 2) ? 64 : 128;
+    const int tiles = (p.N + bn - 1) / bn;
+    const int cs = cluster_for(bn);
+    if (cs >= 2 && bn == 64) {
+      uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.N};
+      uint64_t strides[1] = {(uint64_t)ldb * 2};
+      uint32_t box[2] = {kBK, 64u};
+      int rc = make_tmap_bf16(&tmB, B, 2, dims, strides, box, true);
+      if (rc) return rc;
+    }
     if (cs >= 2) {
-      const int smem = GemmCfg<128>::kSmemBytes;
-      int rc = check_cuda(
-          cudaFuncSetAttribute(gemm_splitk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-          "gemm split-K attr");
+      const int smem = bn == 64 ? GemmCfg<64>::kSmemBytes : GemmCfg<128>::kSmemBytes;
+      auto kern = bn == 64 ? gemm_splitk_kernel<64> : gemm_splitk_kernel<128>;
+      int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                          "gemm split-K attr");
       if (rc) return rc;
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3((unsigned)(tiles * cs), 1, 1);
@@ -1086,7 +1124,7 @@ int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int
       attr[0].val.clusterDim.z = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      rc = check_cuda(cudaLaunchKernelEx(&cfg, gemm_splitk_kernel, tmA, tmB, p), "gemm split-K launch");
+      rc = check_cuda(cudaLaunchKernelEx(&cfg, kern, tmA, tmB, p), "gemm split-K launch");
       if (rc) return rc;
       return check_cuda(cudaGetLastError(), "gemm split-K launch");
     }
