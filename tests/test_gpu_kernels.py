@@ -152,7 +152,7 @@ def test_causal_prefix_ema_op(ops):
     (2, 130, 8, True, 0, 0, 0.9, True), (4, 64, 4, False, 0, 0, 0.9, True), (2, 300, 4, True, 0, 1, 0.9, True),
     (3, 65, 1, True, 7, 40, 0.9, True), (2, 1000, 2, True, 3, 0, 0.9, False), (1, 700, 2, False, 0, 300, 0.5, False),
     (2, 600, 1, True, 0, 0, 0.99, True), (2, 500, 3, True, 2, 0, 0.9, True),
-    (1, 3000, 2, True, 0, 3000, 0.9, True)])
+    (1, 3000, 2, True, 0, 3000, 0.9, True), (3, 32, 3, True, 4, 20, 0.9, False), (2, 7, 2, True, 9, 0, 0.9, True)])
 def test_route_ema_blend_kv(ops, B, T, Hkv, rope, off, T3, beta, with_bias):
     """Stage 1 on y = x [Wk ; Wv]^T: K/V = lam0 y + lam1 EMA(y) (+ lam2 y3) + bias,
     RoPE on K, head-split at token slot t + off; y3 row t is min(t, T3 - 1).
