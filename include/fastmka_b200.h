@@ -214,7 +214,11 @@ FMKA_API int fmka_route_ema_blend_state(const void* x, int64_t x_sb, int64_t x_s
  * (y3_sb, y3_st), row t uses min(t, T3 - 1), y3_st may be 0) and adds
  * lam2 * y3 (logits and b2 then have 3 levels); y3 = NULL for two levels.
  * lam (fp32 [B, T, L]), ema_init / ema_final (fp32 [B, 2*Hkv*128], the state of
- * EMA(y), as for fmka_route_ema_blend_state) may be NULL. */
+ * EMA(y), as for fmka_route_ema_blend_state) may be NULL. The library picks the
+ * scan: token by token for T <= 32, a streaming scan whose CTAs recompute their
+ * incoming state from a warm-up window when |beta| leaves a short memory, else
+ * a chunk-parallel scan with a decoupled look-back; only the last uses the
+ * workspace, which is required all the same. */
 FMKA_API size_t fmka_route_ema_blend_kv_workspace_size(int B, int T, int Hkv);
 FMKA_API int fmka_route_ema_blend_kv(const void* y, int64_t y_sb, int64_t y_st, const float* logits,
                                      const float* b2, const void* y3, int64_t y3_sb, int64_t y3_st, int T3,
