@@ -217,6 +217,32 @@ def _stage_times(fn, steps):
     return {k: sum(v) / len(v) for k, v in acc.items()}
 
 
+def _attention_beside_sdpa(r, flops, reps=5):
+    """This package's attention kernel and torch's SDPA (the reference's default
+    prefill path, mka/layers/fastmka.py:134,157) on the layer's own q/k/v, each
+    timed over `reps` launches queued behind a spin kernel."""
+    from mka_b200 import ops
+
+    q, k, v = r["q"], r["k"], r["v"]
+    runs = {"attn_prefill": lambda: ops.attn_prefill(q, k, v, want_lse=False),
+            "sdpa": lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True,
+                                                                              enable_gqa=True)}
+    out = {}
+    for name, fn in runs.items():
+        fn()
+        torch.cuda.synchronize()
+        torch.cuda._sleep(int(2e8))
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(e) / reps
+        out[name] = {"ms": round(ms, 4), "tflops": round(flops / (ms * 1e-3) / 1e12, 1)}
+    return out
+
+
 def _traffic(name):
     """Per-launch DRAM bytes of a kernel from a committed ncu summary (profiles/)."""
     try:
@@ -309,6 +335,7 @@ def bench_prefill(args, dist, rank, world, device, peaks):
     attn_ms = st.get("attention", float("nan"))
     flops = 4.0 * B * c["H"] * 128 * T * (T + 1) / 2
     achieved = flops / (attn_ms * 1e-3) / 1e12
+    sdpa = _attention_beside_sdpa(fastmka_forward(x, W, c["H"], c["HKV"], 0.9, False, rope=pe), flops)
 
     # end to end through the module with host buffers: every step uploads its
     # input from pinned host memory and downloads the layer output, pipelined
@@ -319,6 +346,7 @@ def bench_prefill(args, dist, rank, world, device, peaks):
     return {
         "ms": ms, "tok_s": tokens / (ms * 1e-3), "e2e_tok_s": tokens / (e2e_ms * 1e-3), "e2e_ms": e2e_ms,
         "h2d": x.numel() * 2, "d2h": x.numel() * 2, "stages_ms": st,
+        "attention_beside_sdpa": sdpa,
         "roofline": {"bound": "tensor", "kernel": "attn_prefill", "achieved": round(achieved, 1),
                      "peak": peaks["bf16"], "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16"], 4),
                      "peak_kind": f"{peaks['src']} burst bf16 (a ~2 ms kernel inside a ms-scale step)",
@@ -940,6 +968,7 @@ def main():
                     "d2h_bytes_per_step": pre["d2h"], "ms_per_step": pre["e2e_ms"],
                     "pipeline": "per sequence: upload of sequence u+1 and download of u-1 overlap the forward of u (3 streams)"},
             "roofline": dict(pre["roofline"], launch_mcycles=mcycles(pre["roofline"]["launch_ms"])),
+            "attention_beside_sdpa": pre["attention_beside_sdpa"],
             "cpu_baseline": cpu,
             "gpu_launches": launches_per_step * args.steps,
             "stages_ms": {k: round(v, 4) for k, v in pre["stages_ms"].items()},
