@@ -111,3 +111,22 @@ def test_store_from_history_feeds_the_attention(ops):
     assert r.shape == (2, 300, 512) and torch.isfinite(r.float()).all()
     layer, p = _gqa_l3_layer(512, 4, 2, 256, 3, seed=27, w_std=0.05)
     _check_gqa_layer(layer, p, x.float(), 4, 2, l3=r.cpu().float())
+
+
+def test_store_append_keeps_chunk_order(ops):
+    """Two banks appended: the chunks of the second follow those of the first, and
+    the recall over the joined bank is the recall over its keys and values."""
+    from mka_b200.l3 import L3ChunkStore
+
+    g = torch.Generator().manual_seed(13)
+    k1, v1 = _bf(40, 256, gen=g).cuda(), _bf(40, 256, gen=g).cuda()
+    k2, v2 = _bf(25, 256, gen=g).cuda(), _bf(25, 256, gen=g).cuda()
+    joined = L3ChunkStore(k1, v1).append(L3ChunkStore(k2, v2))
+    assert joined.n_chunks == 65
+    assert torch.equal(joined.keys[40:], k2) and torch.equal(joined.values[:40], v1)
+    x = _bf(1, 130, 256, gen=g).cuda()
+    r, idx, w = joined.recall_with_indices(x, top_r=6, block_len=64)
+    r2, idx2, w2 = ops.l3_chunk_recall(x, torch.cat([k1, k2]), torch.cat([v1, v2]), 6, 64)
+    assert torch.equal(r, r2) and torch.equal(idx, idx2)
+    with pytest.raises(ValueError):
+        joined.recall(x, top_r=33)
