@@ -125,7 +125,7 @@ struct ScanParams {
   // own segment lengths; whether the L3 / RoPE tensor maps have a batch dimension
   int win_tokens, seg_len_k, seg_len_v, nds_k, n_ctas_k;
   int l3_bcast, rope_bcast;
-  float beta4, beta32;
+  float beta4, beta32;  // kv_window_kernel: beta^(tokens per consumer warp), beta^(tokens per sub-chunk)
 };
 
 __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
@@ -793,16 +793,23 @@ __global__ void __launch_bounds__(kThreads, FMKA_SCAN_MINB) kv_scan_kernel(const
 // During the warm-up each warp keeps its own running sum of its aggregates
 // (A_w = beta^32 A_w + a_w), which needs no barrier; the state at the segment
 // start is sum_w beta^(4 (7 - w)) A_w.
-constexpr int kWinTok = 32;                              // tokens per sub-chunk
+// Tokens per consumer warp: 8 (64-token sub-chunks) halves the barriers and
+// cross-warp combines per token against 4; measured on the layer's scan at
+// batch 4 x 8192: 0.0339 ms against 0.0410 alone, 0.0397 against 0.0448 ms
+// inside the step (batch 2: 0.0205 both).
+#ifndef FMKA_WIN_TPW
+#define FMKA_WIN_TPW 8
+#endif
 constexpr int kWinWarps = 8;                             // consumer warps
-constexpr int kWinTpw = kWinTok / kWinWarps;             // tokens per consumer warp (4)
+constexpr int kWinTpw = FMKA_WIN_TPW;                    // tokens per consumer warp
+constexpr int kWinTok = kWinWarps * kWinTpw;             // tokens per sub-chunk
+constexpr int kWinHalves = kWinTok / 32;                 // gates a producer lane writes per sub-chunk
 constexpr int kWinThreads = (kWinWarps + 1) * 32;
 constexpr int kWinRowBytes = kSlice * 2;                 // one token's 256 channels, bf16
 constexpr int kWinYBytes = kWinTok * kWinRowBytes;       // 16 KB
 constexpr int kWinRopeBytes = kWinTok * 128 * 4;         // 16 KB for cos, 16 KB for sin
 constexpr int kWinGateBytes = kWinTok * 16;             // float4 gate per token
-static_assert(kWinTpw == 4, "kv_window_kernel's powers beta^1..beta^4 assume 4 tokens per consumer warp");
-static_assert(kWinTok == 32, "the producer's lanes compute one gate each");
+static_assert(kWinTpw == 4 || kWinTpw == 8, "4 or 8 tokens per consumer warp");
 constexpr int kWinSmemBudget = 200 * 1024;
 #ifndef FMKA_WIN_WARM_MULTI
 #define FMKA_WIN_WARM_MULTI 1
@@ -902,10 +909,10 @@ __global__ void __launch_bounds__(kWinThreads, 1)
     const int b3 = p.l3_bcast ? 0 : b;
     const int rb = p.rope_bcast ? 0 : b;
     bool dead = false;
-    // router logits of token (segment sub-chunk m) * 32 + lane, loaded S stage uses ahead
+    // router logits of token (segment sub-chunk m) * kWinTok + 32 h + lane, loaded S stage uses ahead
     const float b20 = p.b2 ? p.b2[0] : 0.f, b21 = p.b2 ? p.b2[1] : 0.f, b22 = (kL3 && p.b2) ? p.b2[2] : 0.f;
-    auto load_logits = [&](int m, float (&lg)[3]) {
-      const int t = s0 + m * kWinTok + lane;
+    auto load_logits = [&](int m, int h, float (&lg)[3]) {
+      const int t = s0 + m * kWinTok + 32 * h + lane;
       lg[0] = lg[1] = 0.f;
       lg[2] = -INFINITY;
       if (m >= 0 && t < s1) {
@@ -915,9 +922,12 @@ __global__ void __launch_bounds__(kWinThreads, 1)
         if (kL3) lg[2] = __ldg(src + 2);
       }
     };
-    float lgq[S][3];
+    float lgq[S][kWinHalves][3];
 #pragma unroll
-    for (int a = 0; a < S; ++a) load_logits(a - nwst, lgq[a]);
+    for (int a = 0; a < S; ++a) {
+#pragma unroll
+      for (int h = 0; h < kWinHalves; ++h) load_logits(a - nwst, h, lgq[a][h]);
+    }
     int st = 0;
     uint32_t phase = 0;  // parity of this use of stage st; the previous use had phase ^ 1
     for (int k = 0; k < nsub; ++k) {
@@ -942,28 +952,31 @@ __global__ void __launch_bounds__(kWinThreads, 1)
         }
       }
       if (in_seg) {
-        // gate of token t0 + lane: lam0, lam1 (1 - beta), lam2
-        const int t = t0 + lane;
-        float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t < s1) {
-          float a0 = lgq[0][0] + b20, a1 = lgq[0][1] + b21, a2 = kL3 ? lgq[0][2] + b22 : -INFINITY;
-          const float mx = fmaxf(fmaxf(a0, a1), a2);
-          a0 = __expf(a0 - mx);
-          a1 = __expf(a1 - mx);
-          a2 = kL3 ? __expf(a2 - mx) : 0.f;
-          const float inv = 1.f / (a0 + a1 + a2);
-          a0 *= inv;
-          a1 *= inv;
-          a2 *= inv;
-          if (p.lam != nullptr && ds == 0) {
-            float* dstl = p.lam + ((int64_t)b * T + t) * p.L;
-            dstl[0] = a0;
-            dstl[1] = a1;
-            if (kL3) dstl[2] = a2;
+#pragma unroll
+        for (int h = 0; h < kWinHalves; ++h) {
+          // gate of token t0 + 32 h + lane: lam0, lam1 (1 - beta), lam2
+          const int t = t0 + 32 * h + lane;
+          float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (t < s1) {
+            float a0 = lgq[0][h][0] + b20, a1 = lgq[0][h][1] + b21, a2 = kL3 ? lgq[0][h][2] + b22 : -INFINITY;
+            const float mx = fmaxf(fmaxf(a0, a1), a2);
+            a0 = __expf(a0 - mx);
+            a1 = __expf(a1 - mx);
+            a2 = kL3 ? __expf(a2 - mx) : 0.f;
+            const float inv = 1.f / (a0 + a1 + a2);
+            a0 *= inv;
+            a1 *= inv;
+            a2 *= inv;
+            if (p.lam != nullptr && ds == 0) {
+              float* dstl = p.lam + ((int64_t)b * T + t) * p.L;
+              dstl[0] = a0;
+              dstl[1] = a1;
+              if (kL3) dstl[2] = a2;
+            }
+            g = make_float4(a0, a1 * p.one_minus_beta, a2, 0.f);
           }
-          g = make_float4(a0, a1 * p.one_minus_beta, a2, 0.f);
+          reinterpret_cast<float4*>(stage + Lay::gate)[32 * h + lane] = g;
         }
-        reinterpret_cast<float4*>(stage + Lay::gate)[lane] = g;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&full_bar[st]);
@@ -971,9 +984,13 @@ __global__ void __launch_bounds__(kWinThreads, 1)
 #pragma unroll
       for (int a = 0; a + 1 < S; ++a) {
 #pragma unroll
-        for (int i = 0; i < 3; ++i) lgq[a][i] = lgq[a + 1][i];
+        for (int h = 0; h < kWinHalves; ++h) {
+#pragma unroll
+          for (int i = 0; i < 3; ++i) lgq[a][h][i] = lgq[a + 1][h][i];
+        }
       }
-      load_logits(k + S - nwst, lgq[S - 1]);
+#pragma unroll
+      for (int h = 0; h < kWinHalves; ++h) load_logits(k + S - nwst, h, lgq[S - 1][h]);
       if (++st == S) {
         st = 0;
         phase ^= 1u;
@@ -1003,7 +1020,10 @@ __global__ void __launch_bounds__(kWinThreads, 1)
   }
   const float beta = p.beta;
   const float b4 = p.beta4;
-  const float pw[kWinTpw] = {beta, beta * beta, beta * beta * beta, b4};
+  float pw[kWinTpw];  // beta^(j + 1)
+  pw[0] = beta;
+#pragma unroll
+  for (int j = 1; j < kWinTpw; ++j) pw[j] = pw[j - 1] * beta;
   const int r0 = warp * kWinTpw;  // this warp's first row of a sub-chunk
   bool dead = false;
 
@@ -1061,14 +1081,19 @@ __global__ void __launch_bounds__(kWinThreads, 1)
     if (!dead) dead = !mbar_wait(&full_bar[st], phase, p.status);
     const uint8_t* sb = win_smem + st * Lay::stage;
     const int t0 = s0 + km * kWinTok;
-    float yf[kWinTpw][8];
+    constexpr bool kKeepY = kWinTpw <= 4;  // 8 tokens a warp read y again in the blend (registers)
+    float yf[kKeepY ? kWinTpw : 1][8];
     float u[kWinTpw][8];
 #pragma unroll
     for (int j = 0; j < kWinTpw; ++j) {
       const uint8_t* row = sb + Lay::y + (r0 + j) * kWinRowBytes + col * 2;
-      unpack_lohi(*reinterpret_cast<const uint2*>(row), *reinterpret_cast<const uint2*>(row + 128), yf[j]);
+      float f[8];
+      unpack_lohi(*reinterpret_cast<const uint2*>(row), *reinterpret_cast<const uint2*>(row + 128), f);
 #pragma unroll
-      for (int c = 0; c < 8; ++c) u[j][c] = j == 0 ? yf[j][c] : fmaf(beta, u[j - 1][c], yf[j][c]);
+      for (int c = 0; c < 8; ++c) {
+        u[j][c] = j == 0 ? f[c] : fmaf(beta, u[j - 1][c], f[c]);
+        if constexpr (kKeepY) yf[j][c] = f[c];
+      }
     }
     const int par = km & 1;
     put8(s_agg[par][warp], lane, u[kWinTpw - 1]);
@@ -1110,11 +1135,19 @@ __global__ void __launch_bounds__(kWinThreads, 1)
     for (int j = 0; j < kWinTpw; ++j) {
       const int t = t0 + r0 + j;
       const float4 g = reinterpret_cast<const float4*>(sb + Lay::gate)[r0 + j];
+      float yv[8];
+      if constexpr (kKeepY) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) yv[c] = yf[j][c];
+      } else {
+        const uint8_t* row = sb + Lay::y + (r0 + j) * kWinRowBytes + col * 2;
+        unpack_lohi(*reinterpret_cast<const uint2*>(row), *reinterpret_cast<const uint2*>(row + 128), yv);
+      }
       float o[8];
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const float uc = fmaf(pw[j], s[c], u[j][c]);
-        o[c] = fmaf(g.y, uc, fmaf(g.x, yf[j][c], bias[c]));
+        o[c] = fmaf(g.y, uc, fmaf(g.x, yv[c], bias[c]));
       }
       if (kL3) {
         const int r3 = min(t, p.T3 - 1) - min(t0, p.T3 - 1);
@@ -1294,7 +1327,7 @@ static double win_v_cost() {
   static const double c = [] {
     const char* e = std::getenv("FMKA_WIN_V_COST");
     const double v = e ? std::atof(e) : 0.0;
-    return v > 0.05 && v <= 4.0 ? v : 0.9;  // measured best of 0.5-1.05 at batch 2 and 4 x 8192
+    return v > 0.05 && v <= 4.0 ? v : 0.8;  // measured at batch 2 and 4 x 8192 (0.8-1.0; 0.5-1.05 before)
   }();
   return c;
 }
@@ -1407,7 +1440,7 @@ static int launch_kv_window(ScanParams p, cudaStream_t stream) {
   const int64_t grid = (int64_t)p.n_ctas_k + (int64_t)p.B * nds_v * nseg_v;
   if (grid > 0x7FFFFFFF) return -1;
   p.win_tokens = W;
-  p.beta4 = (float)__builtin_powi((double)p.beta, 4);
+  p.beta4 = (float)__builtin_powi((double)p.beta, kWinTpw);
   p.beta32 = (float)__builtin_powi((double)p.beta, kWinTok);
   const int g = (int)grid;
   if (rope)
