@@ -562,21 +562,27 @@ struct PairCfg {
   static constexpr int kSmemBytesScatter = kSmemBytes + kScatterBytes;
 };
 
-template <bool kScatter>
+// KPS k-blocks per pipeline stage. KPS > 1: each operand of a stage is one 3-D
+// TMA box of KPS k-blocks over a [K/64][rows][64] view of the row-major matrix
+// (A plain row-major, K a multiple of 64), so the producer issues half or a
+// quarter as many boxes; the stage ring keeps the same bytes in flight.
+template <bool kScatter, int KPS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ GemmParams p) {
   using Cfg = PairCfg;
-  constexpr int S = Cfg::kStages;
+  static_assert(Cfg::kStages % KPS == 0, "stages group into whole KPS blocks");
+  constexpr int S = Cfg::kStages / KPS;
   constexpr int BN = Cfg::kBN;
+  constexpr int kA = KPS * Cfg::kABytes;  // A bytes of one stage
+  constexpr int kB = KPS * Cfg::kBBytes;  // B bytes of one stage
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + S * Cfg::kABytes;
-  uint4* sScatter = reinterpret_cast<uint4*>(smem + S * Cfg::kStageBytes);
-  uint64_t* bars =
-      reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes + (kScatter ? Cfg::kScatterBytes : 0));
+  uint8_t* sB = smem + S * kA;
+  uint4* sScatter = reinterpret_cast<uint4*>(smem + S * (kA + kB));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * (kA + kB) + (kScatter ? Cfg::kScatterBytes : 0));
   uint64_t* full = bars;               // [S]  used in the even CTA
   uint64_t* empty = bars + S;          // [S]  both CTAs
   uint64_t* tfull = bars + 2 * S;      // [2]  both CTAs
@@ -634,18 +640,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         gemm_tile_coords(tile, num_m, num_n, p.raster_group, mb, nb);
         const int m0 = mb * (2 * kBM) + (int)rank * kBM;
         const int n0 = nb * BN + (int)rank * Cfg::kHalfN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = 0; kb < num_kb; kb += KPS) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
             *abort_flag = 1;
             break;
           }
-          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (kA + kB));
           const uint32_t fb = full_even + stage * 8;
-          if (p.a_kblk > 0)
-            tma_load_3d_pair(sA + stage * Cfg::kABytes, &tmA, fb, (kb * kBK) % p.a_kblk, m0, (kb * kBK) / p.a_kblk);
-          else
-            tma_load_2d_pair(sA + stage * Cfg::kABytes, &tmA, fb, kb * kBK, m0);
-          tma_load_2d_pair(sB + stage * Cfg::kBBytes, &tmB, fb, kb * kBK, n0);
+          if constexpr (KPS > 1) {
+            tma_load_3d_pair(sA + stage * kA, &tmA, fb, 0, m0, kb);
+            tma_load_3d_pair(sB + stage * kB, &tmB, fb, 0, n0, kb);
+          } else {
+            if (p.a_kblk > 0)
+              tma_load_3d_pair(sA + stage * kA, &tmA, fb, (kb * kBK) % p.a_kblk, m0, (kb * kBK) / p.a_kblk);
+            else
+              tma_load_2d_pair(sA + stage * kA, &tmA, fb, kb * kBK, m0);
+            tma_load_2d_pair(sB + stage * kB, &tmB, fb, kb * kBK, n0);
+          }
           ++issued;
           if (++stage == S) {
             stage = 0;
@@ -681,18 +692,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = 0; kb < num_kb; kb += KPS) {
           if (!mbar_wait(&full[stage], phase, p.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * Cfg::kABytes);
-          const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
+          const uint32_t a_addr = smem_u32(sA + stage * kA);
+          const uint32_t b_addr = smem_u32(sB + stage * kB);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            umma_ss_pair(d_tmem, desc_kmajor_sw128(a_addr + k * 32), desc_kmajor_sw128(b_addr + k * 32), idesc,
-                         (kb | k) != 0);
+          for (int h = 0; h < KPS; ++h) {
+            if (kb + h < num_kb) {  // a box past the last k-block was zero-filled and is skipped
+#pragma unroll
+              for (int k = 0; k < kBK / 16; ++k) {
+                umma_ss_pair(d_tmem, desc_kmajor_sw128(a_addr + h * Cfg::kABytes + k * 32),
+                             desc_kmajor_sw128(b_addr + h * Cfg::kBBytes + k * 32), idesc, ((kb + h) | k) != 0);
+              }
+            }
           }
           tc_commit_pair(&empty[stage], 0x3);
           if (++stage == S) {
@@ -1134,7 +1150,37 @@ int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int
     const int tiles = ((p.M + 2 * kBM - 1) / (2 * kBM)) * ((p.N + PairCfg::kBN - 1) / PairCfg::kBN);
     const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
     const int smem = scatter ? PairCfg::kSmemBytesScatter : PairCfg::kSmemBytes;
-    auto kern = scatter ? gemm_pair_kernel<true> : gemm_pair_kernel<false>;
+    // Two k-blocks per TMA box where A is plain row-major and K is a multiple of
+    // 64; FMKA_GEMM_KPS=1 in the environment keeps one box per k-block.
+    static const bool kps2_enabled = [] {
+      const char* e = std::getenv("FMKA_GEMM_KPS");
+      return e == nullptr || e[0] != '1';
+    }();
+    if (kps2_enabled && !scatter && p.a_kblk == 0 && p.K % kBK == 0) {
+      const int nkb = p.K / kBK;
+      CUtensorMap tA3, tB3;
+      {
+        uint64_t dims[3] = {(uint64_t)kBK, (uint64_t)p.M, (uint64_t)nkb};
+        uint64_t strides[2] = {(uint64_t)lda * 2, (uint64_t)kBK * 2};
+        uint32_t box[3] = {kBK, kBM, 2};
+        int rc = make_tmap_bf16(&tA3, A, 3, dims, strides, box, true);
+        if (rc) return rc;
+      }
+      {
+        uint64_t dims[3] = {(uint64_t)kBK, (uint64_t)p.N, (uint64_t)nkb};
+        uint64_t strides[2] = {(uint64_t)ldb * 2, (uint64_t)kBK * 2};
+        uint32_t box[3] = {kBK, (uint32_t)PairCfg::kHalfN, 2};
+        int rc = make_tmap_bf16(&tB3, B, 3, dims, strides, box, true);
+        if (rc) return rc;
+      }
+      auto kern2 = gemm_pair_kernel<false, 2>;
+      int rc = check_cuda(cudaFuncSetAttribute(kern2, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                          "gemm pair attr");
+      if (rc) return rc;
+      kern2<<<2 * pairs, kThreads, smem, stream>>>(tA3, tB3, p);
+      return check_cuda(cudaGetLastError(), "gemm pair launch");
+    }
+    auto kern = scatter ? gemm_pair_kernel<true, 1> : gemm_pair_kernel<false, 1>;
     int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                         "gemm pair attr");
     if (rc) return rc;
