@@ -795,20 +795,25 @@ constexpr int kSplitMax = 2;
 constexpr int kSplitMax64 = FMKA_SPLITK_MAX64;
 constexpr int split_max_for(int bn) { return bn == 64 ? kSplitMax64 : kSplitMax; }
 
-template <int BN>
+// KPS k-blocks per stage; KPS > 1 loads each operand of a stage as one 3-D TMA
+// box over a [K/64][rows][64] view, as in gemm_pair_kernel.
+template <int BN, int KPS>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ GemmParams p) {
   using Cfg = GemmCfg<BN>;
-  constexpr int S = Cfg::kStages;
+  static_assert(Cfg::kStages % KPS == 0, "stages group into whole KPS blocks");
+  constexpr int S = Cfg::kStages / KPS;
+  constexpr int kA = KPS * Cfg::kABytes;  // A bytes of one stage
+  constexpr int kB = KPS * Cfg::kBBytes;  // B bytes of one stage
   constexpr int kSlotBytes = kSplitRows * BN * 4;  // 32 KB at BN = 128
-  static_assert((split_max_for(BN) - 1) * kSlotBytes <= S * Cfg::kStageBytes, "the partials fit the stage buffers");
+  static_assert((split_max_for(BN) - 1) * kSlotBytes <= S * (kA + kB), "the partials fit the stage buffers");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + S * Cfg::kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint8_t* sB = smem + S * kA;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * (kA + kB));
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* tfull = bars + 2 * S;
@@ -858,17 +863,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       long issued = 0;
-      for (int kb = kb0; kb < kb1 && !*abort_flag; ++kb) {
+      for (int kb = kb0; kb < kb1 && !*abort_flag; kb += KPS) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
           *abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-        if (p.a_kblk > 0)
-          tma_load_3d(sA + stage * Cfg::kABytes, &tmA, &full[stage], (kb * kBK) % p.a_kblk, 0, (kb * kBK) / p.a_kblk);
-        else
-          tma_load_2d(sA + stage * Cfg::kABytes, &tmA, &full[stage], kb * kBK, 0);
-        tma_load_2d(sB + stage * Cfg::kBBytes, &tmB, &full[stage], kb * kBK, n0);
+        mbar_arrive_expect_tx(&full[stage], kA + kB);
+        if constexpr (KPS > 1) {
+          tma_load_3d(sA + stage * kA, &tmA, &full[stage], 0, 0, kb);
+          tma_load_3d(sB + stage * kB, &tmB, &full[stage], 0, n0, kb);
+        } else {
+          if (p.a_kblk > 0)
+            tma_load_3d(sA + stage * kA, &tmA, &full[stage], (kb * kBK) % p.a_kblk, 0, (kb * kBK) / p.a_kblk);
+          else
+            tma_load_2d(sA + stage * kA, &tmA, &full[stage], kb * kBK, 0);
+          tma_load_2d(sB + stage * kB, &tmB, &full[stage], kb * kBK, n0);
+        }
         ++issued;
         if (++stage == S) {
           stage = 0;
@@ -891,18 +901,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int kb = kb0; kb < kb1; ++kb) {
+      for (int kb = kb0; kb < kb1; kb += KPS) {
         if (!mbar_wait(&full[stage], phase, p.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(sA + stage * Cfg::kABytes);
-        const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
+        const uint32_t a_addr = smem_u32(sA + stage * kA);
+        const uint32_t b_addr = smem_u32(sB + stage * kB);
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k) {
-          umma_ss(tmem_base, desc_kmajor_sw128(a_addr + k * 32), desc_kmajor_sw128(b_addr + k * 32), idesc,
-                  (kb > kb0 || k > 0) ? 1u : 0u);
+        for (int h = 0; h < KPS; ++h) {
+          if (kb + h < kb1) {  // a box past this CTA's last k-block is loaded and skipped
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) {
+              umma_ss(tmem_base, desc_kmajor_sw128(a_addr + h * Cfg::kABytes + k * 32),
+                      desc_kmajor_sw128(b_addr + h * Cfg::kBBytes + k * 32), idesc,
+                      (kb + h > kb0 || k > 0) ? 1u : 0u);
+            }
+          }
         }
         tc_commit(&empty[stage]);
         if (++stage == S) {
@@ -1082,6 +1098,13 @@ int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int
     if (rc) return rc;
   }
 
+  // Two k-blocks per TMA box (pair and split-K kernels) where A is plain
+  // row-major and K is a multiple of 64; FMKA_GEMM_KPS=1 in the environment
+  // keeps one box per k-block.
+  static const bool kps2_enabled = [] {
+    const char* e = std::getenv("FMKA_GEMM_KPS");
+    return e == nullptr || e[0] != '1';
+  }();
   // Decode-sized M: split K over a cluster of CTAs per 128-column tile;
   // FMKA_GEMM_SPLITK=0 in the environment keeps one CTA per tile.
   static const bool splitk_enabled = [] {
@@ -1124,7 +1147,22 @@ int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int
     }
     if (cs >= 2) {
       const int smem = bn == 64 ? GemmCfg<64>::kSmemBytes : GemmCfg<128>::kSmemBytes;
-      auto kern = bn == 64 ? gemm_splitk_kernel<64> : gemm_splitk_kernel<128>;
+      const bool kps2 = kps2_enabled && p.a_kblk == 0 && p.K % kBK == 0;
+      if (kps2) {
+        const uint64_t nkb = (uint64_t)(p.K / kBK);
+        uint64_t adims[3] = {(uint64_t)kBK, (uint64_t)p.M, nkb};
+        uint64_t astr[2] = {(uint64_t)lda * 2, (uint64_t)kBK * 2};
+        uint32_t abox[3] = {kBK, kBM, 2};
+        int rc = make_tmap_bf16(&tmA, A, 3, adims, astr, abox, true);
+        if (rc) return rc;
+        uint64_t bdims[3] = {(uint64_t)kBK, (uint64_t)p.N, nkb};
+        uint64_t bstr[2] = {(uint64_t)ldb * 2, (uint64_t)kBK * 2};
+        uint32_t bbox[3] = {kBK, (uint32_t)bn, 2};
+        rc = make_tmap_bf16(&tmB, B, 3, bdims, bstr, bbox, true);
+        if (rc) return rc;
+      }
+      auto kern = bn == 64 ? (kps2 ? gemm_splitk_kernel<64, 2> : gemm_splitk_kernel<64, 1>)
+                           : (kps2 ? gemm_splitk_kernel<128, 2> : gemm_splitk_kernel<128, 1>);
       int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                           "gemm split-K attr");
       if (rc) return rc;
@@ -1150,12 +1188,6 @@ int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int
     const int tiles = ((p.M + 2 * kBM - 1) / (2 * kBM)) * ((p.N + PairCfg::kBN - 1) / PairCfg::kBN);
     const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
     const int smem = scatter ? PairCfg::kSmemBytesScatter : PairCfg::kSmemBytes;
-    // Two k-blocks per TMA box where A is plain row-major and K is a multiple of
-    // 64; FMKA_GEMM_KPS=1 in the environment keeps one box per k-block.
-    static const bool kps2_enabled = [] {
-      const char* e = std::getenv("FMKA_GEMM_KPS");
-      return e == nullptr || e[0] != '1';
-    }();
     if (kps2_enabled && !scatter && p.a_kblk == 0 && p.K % kBK == 0) {
       const int nkb = p.K / kBK;
       CUtensorMap tA3, tB3;
