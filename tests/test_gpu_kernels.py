@@ -43,8 +43,11 @@ def _ref_attn(q, k, v, causal=True, scale=None):
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 384, 256), (1000, 1024, 1024), (77, 136, 3584),
                                    (4096, 2048, 512), (2500, 768, 1536), (40000, 512, 128),
-                                   (64, 6144, 4096), (1, 256, 4096), (50, 384, 576), (33, 1000, 128)])
+                                   (64, 6144, 4096), (1, 256, 4096), (50, 384, 576), (33, 1000, 128),
+                                   (300, 512, 576), (520, 256, 192)])
 def test_gemm_plain(ops, M, N, K):
+    """Includes odd numbers of 64-wide k-blocks (K = 576, 192) on the CTA-pair and
+    split-K kernels, whose last two-k-block box then ends past K and is skipped."""
     g = torch.Generator(device="cuda").manual_seed(M + N + K)
     a = torch.randn(M, K, device="cuda", generator=g).bfloat16()
     w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K)).bfloat16()
